@@ -1,0 +1,97 @@
+// Launch wrappers of the network kernels (implemented in net_kernels.cu and
+// shade.cu). All pointers are device pointers; every wrapper returns the
+// launch's cudaError_t.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace illumina {
+namespace gpu {
+
+enum StorageType { F32 = 0, BF16 = 1 };
+
+struct PreprocessParams {
+  float mean[3], inv_std[3], std[3];
+  float exposure;
+  int decode_srgb;
+};
+
+// frames (layout 0 planar / 1 rgba) -> input (n*S*S*4, storage T), luma (n*S*S
+// f32), scene (n*S*S*4 f32, nullable).
+cudaError_t preprocess(int T, const float *frames, int layout, int n, int S, const PreprocessParams &p,
+                       void *input, float *luma, float *scene, cudaStream_t st);
+
+// Dense conv: src (n,H,W,Cin) -> dst (n,OH,OW,Cout); packed weights [k][k][Cin][Cout].
+cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const float *wpk, const float *bias,
+                 int Cout, int k, int stride, int act, void *dst, cudaStream_t st);
+
+struct GemmOp {
+  int mode;  // 0 pointwise, 1 depthwise->pointwise, 2 lateral
+  const void *src;   // pw: [M][K]; dw: (n,H,W,K); lateral: skip [M][K]
+  const float *w;    // [N][K] f32
+  const float *bias; // [N]
+  const void *res;   // [M][N] or null
+  void *dst;         // [M][N]
+  int n = 1;         // frames
+  int H = 0, W = 0;  // dw: input spatial; lateral: output spatial
+  int OH = 0, OW = 0;// output spatial (dw) ; pw: OH*OW*n = M
+  long M = 0;
+  int N = 0, K = 0;
+  int act = 0, mid_act = 0;
+  int ks = 0, stride = 1;        // dw
+  const float *dw_w = nullptr;   // packed [ks*ks][K]
+  const float *dw_b = nullptr;   // [K]
+  const void *coarse = nullptr;  // lateral: (n, H/2, W/2, N)
+};
+
+cudaError_t gemm(int T, const GemmOp &op, cudaStream_t st);
+
+// Head: src (M,C) storage T -> dst1 (M) f32 disparity (1 channel) and/or
+// dst4 (M*4) f32 broadcast.
+cudaError_t head(int T, const void *src, long M, int C, const float *w, float bias, float *dst1, float *dst4,
+                 cudaStream_t st);
+
+struct BilateralParams {
+  float range_sigma, base_alpha, sensitivity;
+};
+// low1: (n, lh, lw) f32; luma: (n, 2lh, 2lw) f32. dst: (n, 2lh, 2lw) f32.
+// history/out_tex (S*S*4 f32, n must be 1) enable the temporal blend.
+cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *luma, const BilateralParams &p,
+                      float *dst, const float *history, float *out_tex, cudaStream_t st);
+
+// Op-API adaptors: low with channel stride `low_c`, guide with `guide_c`
+// channels of linear colour.
+cudaError_t bilateral_strided(const float *low, int lh, int lw, int low_c, const float *guide, int guide_c,
+                              float range_sigma, float *dst, cudaStream_t st);
+
+// Weight packing (logical .idm layouts -> kernel layouts), optional bf16 rounding.
+cudaError_t pack_dw(const float *w, int C, int k, float *out, int round_bf16, cudaStream_t st);
+cudaError_t pack_conv(const float *w, int O, int I, int k, float *out, int round_bf16, cudaStream_t st);
+cudaError_t copy_round(const float *w, long n, float *out, int round_bf16, cudaStream_t st);
+
+// Expand a 1-channel map to 4 channels (debugTensor of depth_low).
+cudaError_t expand4(const float *src, long n, float *dst4, cudaStream_t st);
+// Convert storage T -> f32.
+cudaError_t to_f32(int T, const void *src, long n, float *dst, cudaStream_t st);
+
+cudaError_t generate_frames(int kind, uint32_t seed0, int n, int S, float *out, cudaStream_t st);
+cudaError_t checksums(const float *maps, int n, long count, uint64_t *sum64, double *fsum, cudaStream_t st);
+
+// Shading (shade.cu)
+struct ShadeParams {
+  float camera[4], toggles[4], ambient[4], misc[4], fog[4], size[4], debug[4], grade[4];
+};
+struct ShadeLight {
+  float position[4], color[4], direction[4], params[4];
+};
+struct ShadeSteps {
+  int contact, ao_dirs, ao_steps, volumetric;
+};
+cudaError_t shade(const float *depth, int dw, int dh, int dch, const float *albedo, int aw, int ah,
+                  const ShadeLight *lights, const ShadeParams &P, const ShadeSteps &steps, int out_w, int out_h,
+                  float *hdr, uint8_t *rgba8, cudaStream_t st);
+cudaError_t resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh, cudaStream_t st);
+
+}  // namespace gpu
+}  // namespace illumina

@@ -1,0 +1,725 @@
+// CUDA kernels of the IlluminaDepth forward pass (sm_100a).
+//
+// Layout: every activation is channels-last with the batch outermost,
+// (n, y, x, c), c a multiple of 4, stored as float32 or bfloat16 (`T`); all
+// arithmetic accumulates in float32. The op semantics are the reference's
+// (src/model/reference.ts): residual added before the activation, the
+// depthwise result activated before the pointwise, bilinear taps clamped
+// independently, sigmoid head broadcast, 3x3 joint-bilateral upsample.
+//
+// The pointwise-shaped ops (pw, dw->pw, lateral) share one register-blocked
+// tile GEMM: a CTA owns BM output pixels x BN output channels, walks the input
+// channels in chunks of 16 staged through shared memory, and fuses the
+// operand producer (plain load, depthwise k x k + bias + activation, or the
+// skip tensor) and the epilogue (bias, residual / bilinear-upsampled coarse,
+// activation) so no intermediate reaches HBM.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+
+namespace illumina {
+namespace gpu {
+
+// ---------------------------------------------------------------------------
+// helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float act_apply(int act, float v) {
+  switch (act) {
+    case 1: return fmaxf(v, 0.0f);
+    case 2: return fminf(fmaxf(v, 0.0f), 6.0f);
+    case 3: return (v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)) / 6.0f;
+    default: return v;
+  }
+}
+
+template <typename T>
+struct Io;
+
+template <>
+struct Io<float> {
+  static __device__ __forceinline__ float4 load4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+  static __device__ __forceinline__ void store4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+  static __device__ __forceinline__ float2 load2(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+  static __device__ __forceinline__ void store2(float *p, float2 v) { *reinterpret_cast<float2 *>(p) = v; }
+};
+
+template <>
+struct Io<__nv_bfloat16> {
+  static __device__ __forceinline__ float4 load4(const __nv_bfloat16 *p) {
+    uint2 r = *reinterpret_cast<const uint2 *>(p);
+    __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162 *>(&r.x), b = *reinterpret_cast<__nv_bfloat162 *>(&r.y);
+    float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+    return make_float4(fa.x, fa.y, fb.x, fb.y);
+  }
+  static __device__ __forceinline__ void store4(__nv_bfloat16 *p, float4 v) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 r;
+    r.x = *reinterpret_cast<uint32_t *>(&a);
+    r.y = *reinterpret_cast<uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(p) = r;
+  }
+  static __device__ __forceinline__ float2 load2(const __nv_bfloat16 *p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
+  }
+  static __device__ __forceinline__ void store2(__nv_bfloat16 *p, float2 v) {
+    *reinterpret_cast<__nv_bfloat162 *>(p) = __floats2bfloat162_rn(v.x, v.y);
+  }
+};
+
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float4 f4fma(float4 a, float4 b, float4 c) {
+  return make_float4(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y), fmaf(a.z, b.z, c.z), fmaf(a.w, b.w, c.w));
+}
+
+__device__ __forceinline__ float srgb_to_linear(float c) {
+  return c <= 0.04045f ? c / 12.92f : powf((c + 0.055f) / 1.055f, 2.4f);
+}
+
+static inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+// ---------------------------------------------------------------------------
+// preprocess (src/model/kernels/io.ts:64-118 semantics, refPreprocess)
+// ---------------------------------------------------------------------------
+
+template <typename T>
+__global__ void k_preprocess(const float *__restrict__ frames, int layout, long total, int S, PreprocessParams p,
+                             T *__restrict__ input, float *__restrict__ luma, float *__restrict__ scene) {
+  long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  long plane = (long)S * S;
+  long b = idx / plane, pix = idx - b * plane;
+  float r, g, bl;
+  if (layout == 0) {
+    const float *f = frames + b * 3 * plane + pix;
+    r = __ldg(f), g = __ldg(f + plane), bl = __ldg(f + 2 * plane);
+  } else {
+    float4 v = __ldg(reinterpret_cast<const float4 *>(frames) + idx);
+    r = v.x, g = v.y, bl = v.z;
+  }
+  if (p.decode_srgb) r = srgb_to_linear(r), g = srgb_to_linear(g), bl = srgb_to_linear(bl);
+  r *= p.exposure, g *= p.exposure, bl *= p.exposure;
+  float l = 0.2126f * r + 0.7152f * g + 0.0722f * bl;
+  float4 o = make_float4((r - p.mean[0]) / p.std[0], (g - p.mean[1]) / p.std[1], (bl - p.mean[2]) / p.std[2], l);
+  Io<T>::store4(input + idx * 4, o);
+  if (luma) luma[idx] = l;
+  if (scene) reinterpret_cast<float4 *>(scene)[idx] = make_float4(r, g, bl, 1.0f);
+}
+
+cudaError_t preprocess(int T, const float *frames, int layout, int n, int S, const PreprocessParams &p, void *input,
+                       float *luma, float *scene, cudaStream_t st) {
+  long total = (long)n * S * S;
+  if (total == 0) return cudaSuccess;
+  if (T == F32)
+    k_preprocess<float><<<blocks_for(total, 256), 256, 0, st>>>(frames, layout, total, S, p, (float *)input, luma,
+                                                                scene);
+  else
+    k_preprocess<__nv_bfloat16><<<blocks_for(total, 256), 256, 0, st>>>(frames, layout, total, S, p,
+                                                                         (__nv_bfloat16 *)input, luma, scene);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// dense k x k conv (stem): one thread = one output pixel x 16 channels
+// ---------------------------------------------------------------------------
+
+template <typename T>
+__global__ void k_conv(const T *__restrict__ src, int n, int H, int W, int Cin, const float *__restrict__ wpk,
+                       const float *__restrict__ bias, int Cout, int k, int stride, int act, int OH, int OW,
+                       T *__restrict__ dst) {
+  long pix = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  long total = (long)n * OH * OW;
+  if (pix >= total) return;
+  int og = blockIdx.y;  // group of 16 output channels
+  int ox = (int)(pix % OW);
+  long t = pix / OW;
+  int oy = (int)(t % OH);
+  int b = (int)(t / OH);
+  int pad = (k - 1) >> 1;
+  int cout4 = Cout >> 2, cin4 = Cin >> 2;
+  int g0 = og * 4;
+  float4 acc[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    int g = g0 + j;
+    acc[j] = g < cout4 ? __ldg(reinterpret_cast<const float4 *>(bias) + g) : make_float4(0, 0, 0, 0);
+  }
+  for (int ky = 0; ky < k; ky++) {
+    int iy = oy * stride + ky - pad;
+    if (iy < 0 || iy >= H) continue;
+    for (int kx = 0; kx < k; kx++) {
+      int ix = ox * stride + kx - pad;
+      if (ix < 0 || ix >= W) continue;
+      const T *px = src + (((long)b * H + iy) * W + ix) * Cin;
+      const float4 *wk = reinterpret_cast<const float4 *>(wpk) + (long)(ky * k + kx) * Cin * cout4;
+      for (int c4 = 0; c4 < cin4; c4++) {
+        float4 x = Io<T>::load4(px + c4 * 4);
+        float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float4 *wr = wk + (long)(c4 * 4 + q) * cout4;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            int g = g0 + j;
+            if (g < cout4) acc[j] = f4fma(make_float4(xs[q], xs[q], xs[q], xs[q]), __ldg(wr + g), acc[j]);
+          }
+        }
+      }
+    }
+  }
+  T *o = dst + pix * Cout;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    int g = g0 + j;
+    if (g < cout4) {
+      float4 v = acc[j];
+      v = make_float4(act_apply(act, v.x), act_apply(act, v.y), act_apply(act, v.z), act_apply(act, v.w));
+      Io<T>::store4(o + g * 4, v);
+    }
+  }
+}
+
+cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const float *wpk, const float *bias, int Cout,
+                 int k, int stride, int act, void *dst, cudaStream_t st) {
+  int pad = (k - 1) >> 1;
+  int OH = (H + 2 * pad - k) / stride + 1, OW = (W + 2 * pad - k) / stride + 1;
+  long total = (long)n * OH * OW;
+  if (total <= 0) return cudaSuccess;
+  dim3 grid(blocks_for(total, 128), (Cout / 4 + 3) / 4);
+  if (T == F32)
+    k_conv<float><<<grid, 128, 0, st>>>((const float *)src, n, H, W, Cin, wpk, bias, Cout, k, stride, act, OH, OW,
+                                        (float *)dst);
+  else
+    k_conv<__nv_bfloat16><<<grid, 128, 0, st>>>((const __nv_bfloat16 *)src, n, H, W, Cin, wpk, bias, Cout, k, stride,
+                                                act, OH, OW, (__nv_bfloat16 *)dst);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// tile GEMM for pw / dw->pw / lateral
+// ---------------------------------------------------------------------------
+
+constexpr int GBK = 16;       // input channels per chunk
+constexpr int GTHREADS = 256; // 16 x 16 thread grid
+
+struct GemmParams {
+  const void *src;
+  const float *w, *bias;
+  const void *res;
+  void *dst;
+  const float *dw_w, *dw_b;
+  const void *coarse;
+  long M;
+  int N, K, act, mid_act;
+  int H, W, OH, OW, stride;  // dw input dims / output dims; lateral output dims in OH, OW
+};
+
+// MODE 0: pointwise; 1: depthwise KS x KS then pointwise; 2: lateral
+template <typename T, int BM, int BN, int MODE, int KS>
+__global__ void __launch_bounds__(GTHREADS) k_gemm(const GemmParams p) {
+  constexpr int TM = BM / 16, TN = BN / 16;
+  constexpr int A_VEC = BM * 4;  // float4 groups per chunk (BM pixels x 4 channel groups)
+  constexpr int A_PER = (A_VEC + GTHREADS - 1) / GTHREADS;
+  constexpr int B_VEC = BN * 4;
+  constexpr int B_PER = (B_VEC + GTHREADS - 1) / GTHREADS;
+  __shared__ __align__(16) float As[GBK][BM + 4];
+  __shared__ __align__(16) float Bs[GBK][BN + 4];
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const long m0 = (long)blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+  const int K4 = p.K >> 2;
+
+  // Per-thread A-producer coordinates (fixed across chunks).
+  int a_mm[A_PER], a_kq[A_PER];
+  bool a_ok[A_PER];
+  int a_b[A_PER], a_y[A_PER], a_x[A_PER];
+#pragma unroll
+  for (int i = 0; i < A_PER; i++) {
+    int v = tid + i * GTHREADS;
+    a_mm[i] = v >> 2;
+    a_kq[i] = v & 3;
+    long m = m0 + a_mm[i];
+    a_ok[i] = (v < A_VEC) && (m < p.M);
+    a_b[i] = a_y[i] = a_x[i] = 0;
+    if (MODE == 1 && a_ok[i]) {
+      a_x[i] = (int)(m % p.OW);
+      long t = m / p.OW;
+      a_y[i] = (int)(t % p.OH);
+      a_b[i] = (int)(t / p.OH);
+    }
+  }
+
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; i++)
+#pragma unroll
+    for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
+
+  const T *src = reinterpret_cast<const T *>(p.src);
+  for (int k0 = 0; k0 < p.K; k0 += GBK) {
+    // ---- produce the A chunk (BM x 16) ----
+#pragma unroll
+    for (int i = 0; i < A_PER; i++) {
+      float4 v = make_float4(0, 0, 0, 0);
+      int c4 = (k0 >> 2) + a_kq[i];
+      if (a_ok[i] && c4 < K4) {
+        if (MODE != 1) {
+          v = Io<T>::load4(src + (m0 + a_mm[i]) * p.K + c4 * 4);
+        } else {
+          constexpr int pad = (KS - 1) / 2;
+          float4 s = __ldg(reinterpret_cast<const float4 *>(p.dw_b) + c4);
+#pragma unroll
+          for (int ky = 0; ky < KS; ky++) {
+            int iy = a_y[i] * p.stride + ky - pad;
+            if (iy < 0 || iy >= p.H) continue;
+            const T *row = src + ((long)a_b[i] * p.H + iy) * p.W * p.K;
+#pragma unroll
+            for (int kx = 0; kx < KS; kx++) {
+              int ix = a_x[i] * p.stride + kx - pad;
+              if (ix < 0 || ix >= p.W) continue;
+              float4 x = Io<T>::load4(row + (long)ix * p.K + c4 * 4);
+              float4 w = __ldg(reinterpret_cast<const float4 *>(p.dw_w) + (long)(ky * KS + kx) * K4 + c4);
+              s = f4fma(x, w, s);
+            }
+          }
+          v = make_float4(act_apply(p.mid_act, s.x), act_apply(p.mid_act, s.y), act_apply(p.mid_act, s.z),
+                          act_apply(p.mid_act, s.w));
+        }
+      }
+      if (tid + i * GTHREADS < A_VEC) {
+        int kk = a_kq[i] * 4, mm = a_mm[i];
+        As[kk + 0][mm] = v.x;
+        As[kk + 1][mm] = v.y;
+        As[kk + 2][mm] = v.z;
+        As[kk + 3][mm] = v.w;
+      }
+    }
+    // ---- B chunk (BN x 16) from w[N][K] ----
+#pragma unroll
+    for (int i = 0; i < B_PER; i++) {
+      int v = tid + i * GTHREADS;
+      if (v < B_VEC) {
+        int nn = v >> 2, kq = v & 3;
+        int n = n0 + nn, c4 = (k0 >> 2) + kq;
+        float4 w = make_float4(0, 0, 0, 0);
+        if (n < p.N && c4 < K4) w = __ldg(reinterpret_cast<const float4 *>(p.w + (long)n * p.K) + c4);
+        int kk = kq * 4;
+        Bs[kk + 0][nn] = w.x;
+        Bs[kk + 1][nn] = w.y;
+        Bs[kk + 2][nn] = w.z;
+        Bs[kk + 3][nn] = w.w;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < GBK; kk++) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int i = 0; i < TM; i += 2) {
+        float2 t = *reinterpret_cast<const float2 *>(&As[kk][ty * TM + i]);
+        a[i] = t.x, a[i + 1] = t.y;
+      }
+#pragma unroll
+      for (int j = 0; j < TN; j += 2) {
+        float2 t = *reinterpret_cast<const float2 *>(&Bs[kk][tx * TN + j]);
+        b[j] = t.x, b[j + 1] = t.y;
+      }
+#pragma unroll
+      for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+
+  // ---- epilogue ----
+  const T *res = reinterpret_cast<const T *>(p.res);
+  const T *coarse = reinterpret_cast<const T *>(p.coarse);
+  T *dst = reinterpret_cast<T *>(p.dst);
+#pragma unroll
+  for (int i = 0; i < TM; i++) {
+    long m = m0 + ty * TM + i;
+    if (m >= p.M) continue;
+    int ly0 = 0, ly1 = 0, lx0 = 0, lx1 = 0, lb = 0;
+    float fx = 0, fy = 0;
+    if (MODE == 2) {
+      // refUpsample2 (reference.ts:161-193): source coord (i + 0.5) / 2 - 0.5,
+      // both taps from the unclamped floor, clamped independently.
+      int x = (int)(m % p.OW);
+      long t = m / p.OW;
+      int y = (int)(t % p.OH);
+      lb = (int)(t / p.OH);
+      int CH = p.OH >> 1, CW = p.OW >> 1;
+      float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
+      float fy0 = floorf(sy), fx0 = floorf(sx);
+      fy = sy - fy0, fx = sx - fx0;
+      ly0 = min(max((int)fy0, 0), CH - 1), ly1 = min(max((int)fy0 + 1, 0), CH - 1);
+      lx0 = min(max((int)fx0, 0), CW - 1), lx1 = min(max((int)fx0 + 1, 0), CW - 1);
+      long rb = (long)lb * CH;
+      ly0 = (int)((rb + ly0) * CW), ly1 = (int)((rb + ly1) * CW);  // row base pixel indices
+    }
+#pragma unroll
+    for (int j = 0; j < TN; j += 2) {
+      int n = n0 + tx * TN + j;
+      if (n >= p.N) continue;
+      float2 v = make_float2(acc[i][j] + __ldg(p.bias + n), acc[i][j + 1] + __ldg(p.bias + n + 1));
+      if (MODE == 2) {
+        long CW = p.OW >> 1;
+        (void)CW;
+        float2 a = Io<T>::load2(coarse + ((long)ly0 + lx0) * p.N + n);
+        float2 b = Io<T>::load2(coarse + ((long)ly0 + lx1) * p.N + n);
+        float2 c = Io<T>::load2(coarse + ((long)ly1 + lx0) * p.N + n);
+        float2 d = Io<T>::load2(coarse + ((long)ly1 + lx1) * p.N + n);
+        float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
+        v.x += a.x * w00 + b.x * w01 + c.x * w10 + d.x * w11;
+        v.y += a.y * w00 + b.y * w01 + c.y * w10 + d.y * w11;
+      }
+      if (res) {
+        float2 r = Io<T>::load2(res + m * p.N + n);
+        v.x += r.x, v.y += r.y;
+      }
+      v.x = act_apply(p.act, v.x);
+      v.y = act_apply(p.act, v.y);
+      Io<T>::store2(dst + m * p.N + n, v);
+    }
+  }
+}
+
+template <typename T, int MODE, int KS>
+static cudaError_t launch_gemm_t(const GemmParams &p, cudaStream_t st) {
+  // Tile choice: wide N tiles amortise the dw producer; shrink BM until the
+  // grid covers the 148 SMs at least twice.
+  auto ctas = [&](int bm, int bn) { return ((p.M + bm - 1) / bm) * (long)((p.N + bn - 1) / bn); };
+  int bn = p.N <= 32 ? 32 : 64;
+  if (MODE == 1 && p.N > 64) bn = 128;
+  int bm = 128;
+  while (bm > 32 && ctas(bm, bn) < 296) bm >>= 1;
+  dim3 grid((unsigned)((p.M + bm - 1) / bm), (unsigned)((p.N + bn - 1) / bn));
+#define ILL_GEMM_CASE(BM_, BN_)                                      \
+  if (bm == BM_ && bn == BN_) {                                      \
+    k_gemm<T, BM_, BN_, MODE, KS><<<grid, GTHREADS, 0, st>>>(p);     \
+    return cudaGetLastError();                                       \
+  }
+  ILL_GEMM_CASE(128, 32) ILL_GEMM_CASE(64, 32) ILL_GEMM_CASE(32, 32)
+  ILL_GEMM_CASE(128, 64) ILL_GEMM_CASE(64, 64) ILL_GEMM_CASE(32, 64)
+  if (MODE == 1) { ILL_GEMM_CASE(128, 128) ILL_GEMM_CASE(64, 128) ILL_GEMM_CASE(32, 128) }
+#undef ILL_GEMM_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
+template <typename T>
+static cudaError_t gemm_t(const GemmOp &op, cudaStream_t st) {
+  GemmParams p;
+  p.src = op.src, p.w = op.w, p.bias = op.bias, p.res = op.res, p.dst = op.dst;
+  p.dw_w = op.dw_w, p.dw_b = op.dw_b, p.coarse = op.coarse;
+  p.M = op.M, p.N = op.N, p.K = op.K, p.act = op.act, p.mid_act = op.mid_act;
+  p.H = op.H, p.W = op.W, p.OH = op.OH, p.OW = op.OW, p.stride = op.stride;
+  if (p.M <= 0) return cudaSuccess;
+  if (op.mode == 0) return launch_gemm_t<T, 0, 1>(p, st);
+  if (op.mode == 2) return launch_gemm_t<T, 2, 1>(p, st);
+  if (op.ks == 3) return launch_gemm_t<T, 1, 3>(p, st);
+  if (op.ks == 5) return launch_gemm_t<T, 1, 5>(p, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t gemm(int T, const GemmOp &op, cudaStream_t st) {
+  return T == F32 ? gemm_t<float>(op, st) : gemm_t<__nv_bfloat16>(op, st);
+}
+
+// ---------------------------------------------------------------------------
+// head (io.ts:141-166): sigmoid(b + w . x)
+// ---------------------------------------------------------------------------
+
+template <typename T>
+__global__ void k_head(const T *__restrict__ src, long M, int C, const float *__restrict__ w, float bias,
+                       float *__restrict__ dst1, float *__restrict__ dst4) {
+  long m = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float s = bias;
+  const T *x = src + m * C;
+  for (int c = 0; c < C; c += 4) {
+    float4 v = Io<T>::load4(x + c);
+    float4 q = __ldg(reinterpret_cast<const float4 *>(w + c));
+    s = fmaf(v.x, q.x, s);
+    s = fmaf(v.y, q.y, s);
+    s = fmaf(v.z, q.z, s);
+    s = fmaf(v.w, q.w, s);
+  }
+  float d = 1.0f / (1.0f + expf(-s));
+  if (dst1) dst1[m] = d;
+  if (dst4) reinterpret_cast<float4 *>(dst4)[m] = make_float4(d, d, d, d);
+}
+
+cudaError_t head(int T, const void *src, long M, int C, const float *w, float bias, float *dst1, float *dst4,
+                 cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  if (T == F32)
+    k_head<float><<<blocks_for(M, 256), 256, 0, st>>>((const float *)src, M, C, w, bias, dst1, dst4);
+  else
+    k_head<__nv_bfloat16><<<blocks_for(M, 256), 256, 0, st>>>((const __nv_bfloat16 *)src, M, C, w, bias, dst1,
+                                                              dst4);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// joint-bilateral upsample + temporal blend (io.ts:203-283)
+// ---------------------------------------------------------------------------
+
+// low: (n, lh, lw) with channel stride lc; guide luma either precomputed
+// (luma, 1 channel) or from linear colour (guide, gc channels).
+__global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh, int lw,
+                            const float *__restrict__ luma, const float *__restrict__ guide, int gc,
+                            BilateralParams p, float *__restrict__ dst, const float *__restrict__ history,
+                            float *__restrict__ out_tex) {
+  int S = lh * 2, SW = lw * 2;
+  long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  long total = (long)n * S * SW;
+  if (idx >= total) return;
+  int x = (int)(idx % SW);
+  long t = idx / SW;
+  int y = (int)(t % S);
+  int b = (int)(t / S);
+  auto luma_at = [&](int gx, int gy) -> float {
+    long g = ((long)b * S + gy) * SW + gx;
+    if (luma) return __ldg(luma + g);
+    const float *c = guide + g * gc;
+    return 0.2126f * __ldg(c) + 0.7152f * __ldg(c + 1) + 0.0722f * __ldg(c + 2);
+  };
+  float here = luma_at(x, y);
+  float cx = (x + 0.5f) * 0.5f - 0.5f, cy = (y + 0.5f) * 0.5f - 0.5f;
+  int bx = (int)floorf(cx + 0.5f), by = (int)floorf(cy + 0.5f);
+  float inv = 1.0f / fmaxf(p.range_sigma, 1e-4f);
+  float weighted = 0.0f, total_w = 0.0f;
+#pragma unroll
+  for (int dy = -1; dy <= 1; dy++)
+#pragma unroll
+    for (int dx = -1; dx <= 1; dx++) {
+      int qx = min(max(bx + dx, 0), lw - 1), qy = min(max(by + dy, 0), lh - 1);
+      float disp = __ldg(low + (((long)b * lh + qy) * lw + qx) * lc);
+      float there = luma_at(qx * 2, qy * 2);
+      float dxs = qx - cx, dys = qy - cy;
+      float spatial = expf(-(dxs * dxs + dys * dys) * 0.5f);
+      float dl = (here - there) * inv;
+      float wgt = spatial * expf(-dl * dl * 0.5f);
+      weighted = fmaf(disp, wgt, weighted);
+      total_w += wgt;
+    }
+  float up = weighted / fmaxf(total_w, 1e-6f);
+  float out = up;
+  if (out_tex) {
+    float4 prev = history ? reinterpret_cast<const float4 *>(history)[idx] : make_float4(0, 0, 0, 0);
+    float change = fabsf(up - prev.x);
+    float alpha = prev.w < 0.5f ? 1.0f : fminf(fmaxf(p.base_alpha + change * p.sensitivity, p.base_alpha), 1.0f);
+    out = prev.x + (up - prev.x) * alpha;
+    reinterpret_cast<float4 *>(out_tex)[idx] = make_float4(out, up, change, 1.0f);
+  }
+  if (dst) dst[idx] = out;
+}
+
+cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *luma, const BilateralParams &p,
+                      float *dst, const float *history, float *out_tex, cudaStream_t st) {
+  long total = (long)n * lh * lw * 4;
+  if (total == 0) return cudaSuccess;
+  k_bilateral<<<blocks_for(total, 256), 256, 0, st>>>(low1, 1, n, lh, lw, luma, nullptr, 0, p, dst, history,
+                                                      out_tex);
+  return cudaGetLastError();
+}
+
+cudaError_t bilateral_strided(const float *low, int lh, int lw, int low_c, const float *guide, int guide_c,
+                              float range_sigma, float *dst, cudaStream_t st) {
+  long total = (long)lh * lw * 4;
+  if (total == 0) return cudaSuccess;
+  BilateralParams p{range_sigma, 0.35f, 3.0f};
+  k_bilateral<<<blocks_for(total, 256), 256, 0, st>>>(low, low_c, 1, lh, lw, nullptr, guide, guide_c, p, dst,
+                                                      nullptr, nullptr);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// weight packing
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float maybe_bf16(float v, int r) {
+  return r ? __bfloat162float(__float2bfloat16_rn(v)) : v;
+}
+
+// [C][k][k] -> [k*k][C]
+__global__ void k_pack_dw(const float *w, int C, int k, float *out, int r) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  int kk = k * k;
+  if (i >= C * kk) return;
+  int c = i / kk, t = i % kk;
+  out[t * C + c] = maybe_bf16(w[i], r);
+}
+
+// [O][I][k][k] -> [k][k][I][O]
+__global__ void k_pack_conv(const float *w, int O, int I, int k, float *out, int r) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  int total = O * I * k * k;
+  if (i >= total) return;
+  int kx = i % k, ky = (i / k) % k, ic = (i / (k * k)) % I, oc = i / (k * k * I);
+  out[((ky * k + kx) * I + ic) * O + oc] = maybe_bf16(w[i], r);
+}
+
+__global__ void k_copy_round(const float *w, long n, float *out, int r) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = maybe_bf16(w[i], r);
+}
+
+cudaError_t pack_dw(const float *w, int C, int k, float *out, int r, cudaStream_t st) {
+  k_pack_dw<<<blocks_for((long)C * k * k, 256), 256, 0, st>>>(w, C, k, out, r);
+  return cudaGetLastError();
+}
+cudaError_t pack_conv(const float *w, int O, int I, int k, float *out, int r, cudaStream_t st) {
+  k_pack_conv<<<blocks_for((long)O * I * k * k, 256), 256, 0, st>>>(w, O, I, k, out, r);
+  return cudaGetLastError();
+}
+cudaError_t copy_round(const float *w, long n, float *out, int r, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_copy_round<<<blocks_for(n, 256), 256, 0, st>>>(w, n, out, r);
+  return cudaGetLastError();
+}
+
+__global__ void k_expand4(const float *src, long n, float *dst4) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    float v = src[i];
+    reinterpret_cast<float4 *>(dst4)[i] = make_float4(v, v, v, v);
+  }
+}
+cudaError_t expand4(const float *src, long n, float *dst4, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  k_expand4<<<blocks_for(n, 256), 256, 0, st>>>(src, n, dst4);
+  return cudaGetLastError();
+}
+
+__global__ void k_bf16_to_f32(const __nv_bfloat16 *src, long n, float *dst) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = __bfloat162float(src[i]);
+}
+cudaError_t to_f32(int T, const void *src, long n, float *dst, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (T == F32) return cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, st);
+  k_bf16_to_f32<<<blocks_for(n, 256), 256, 0, st>>>((const __nv_bfloat16 *)src, n, dst);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// synthetic frames and checksums
+// ---------------------------------------------------------------------------
+
+// mulberry32 output for absolute draw index j (0-based) of the stream seeded
+// with `seed`: the state after j+1 increments is seed + (j+1)*0x6d2b79f5.
+__device__ __forceinline__ double mb32_at(uint32_t seed, uint32_t j) {
+  uint32_t t = seed + (j + 1u) * 0x6d2b79f5u;
+  t = (t ^ (t >> 15)) * (t | 1u);
+  t ^= t + (t ^ (t >> 7)) * (t | 61u);
+  return (double)(t ^ (t >> 14)) / 4294967296.0;
+}
+
+__global__ void k_gen_uniform(uint32_t seed0, int n, int S, float *out) {
+  long per = 3L * S * S;
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= per * n) return;
+  int f = (int)(i / per);
+  uint32_t j = (uint32_t)(i - (long)f * per);
+  out[i] = (float)mb32_at(seed0 + (uint32_t)f, j);
+}
+
+// Blob frames: per channel 8 blobs (cx, cy in [0,S), sx, sy in [20,120],
+// theta in [0,pi), amplitude in [0,1]) = 144 draws, then per value a
+// Box-Muller N(0, 0.02) noise sample (2 draws) in (c, y, x) order.
+__global__ void k_gen_blobs(uint32_t seed0, int n, int S, float *out) {
+  long per = 3L * S * S;
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= per * n) return;
+  int f = (int)(i / per);
+  long j = i - (long)f * per;
+  int c = (int)(j / ((long)S * S));
+  long pix = j - (long)c * S * S;
+  int y = (int)(pix / S), x = (int)(pix % S);
+  uint32_t seed = seed0 + (uint32_t)f;
+  float v = 0.0f;
+  for (int bidx = 0; bidx < 8; bidx++) {
+    uint32_t d = (uint32_t)((c * 8 + bidx) * 6);
+    float cxp = (float)(mb32_at(seed, d) * S), cyp = (float)(mb32_at(seed, d + 1) * S);
+    float sx = (float)(20.0 + 100.0 * mb32_at(seed, d + 2)), sy = (float)(20.0 + 100.0 * mb32_at(seed, d + 3));
+    float th = (float)(M_PI * mb32_at(seed, d + 4));
+    float amp = (float)mb32_at(seed, d + 5);
+    float dx = x + 0.5f - cxp, dy = y + 0.5f - cyp;
+    float cs = cosf(th), sn = sinf(th);
+    float u = cs * dx + sn * dy, w = -sn * dx + cs * dy;
+    v += amp * expf(-0.5f * (u * u / (sx * sx) + w * w / (sy * sy)));
+  }
+  uint32_t nd = 144u + 2u * (uint32_t)j;
+  double uu = mb32_at(seed, nd);
+  if (uu < 1e-9) uu = 1e-9;
+  double vv = mb32_at(seed, nd + 1);
+  float g = (float)(sqrt(-2.0 * log(uu)) * cos(2.0 * M_PI * vv));
+  v += 0.02f * g;
+  out[i] = fminf(fmaxf(v, 0.0f), 1.0f);
+}
+
+cudaError_t generate_frames(int kind, uint32_t seed0, int n, int S, float *out, cudaStream_t st) {
+  long total = 3L * S * S * n;
+  if (total == 0) return cudaSuccess;
+  if (kind == 0) k_gen_uniform<<<blocks_for(total, 256), 256, 0, st>>>(seed0, n, S, out);
+  else k_gen_blobs<<<blocks_for(total, 256), 256, 0, st>>>(seed0, n, S, out);
+  return cudaGetLastError();
+}
+
+__global__ void k_checksums(const float *maps, long count, unsigned long long *sum64, double *fsum) {
+  int f = blockIdx.y;
+  const uint32_t *bits = reinterpret_cast<const uint32_t *>(maps + (long)f * count);
+  const float *vals = maps + (long)f * count;
+  unsigned long long h = 0;
+  double s = 0.0;
+  for (long j = (long)blockIdx.x * blockDim.x + threadIdx.x; j < count; j += (long)gridDim.x * blockDim.x) {
+    h += (unsigned long long)bits[j] * (unsigned long long)(2 * j + 1);
+    s += (double)vals[j];
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    h += __shfl_down_sync(0xffffffffu, h, o);
+    s += __shfl_down_sync(0xffffffffu, s, o);
+  }
+  __shared__ unsigned long long hs[32];
+  __shared__ double ss[32];
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) hs[wid] = h, ss[wid] = s;
+  __syncthreads();
+  if (wid == 0) {
+    int nw = blockDim.x >> 5;
+    h = lane < nw ? hs[lane] : 0ull;
+    s = lane < nw ? ss[lane] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) {
+      h += __shfl_down_sync(0xffffffffu, h, o);
+      s += __shfl_down_sync(0xffffffffu, s, o);
+    }
+    if (lane == 0) {
+      atomicAdd(sum64 + f, h);
+      atomicAdd(fsum + f, s);
+    }
+  }
+}
+
+cudaError_t checksums(const float *maps, int n, long count, uint64_t *sum64, double *fsum, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  cudaError_t e = cudaMemsetAsync(sum64, 0, sizeof(uint64_t) * n, st);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(fsum, 0, sizeof(double) * n, st);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((count + 255) / 256 < 64 ? (count + 255) / 256 : 64), n);
+  if (grid.x == 0) grid.x = 1;
+  k_checksums<<<grid, 256, 0, st>>>(maps, count, (unsigned long long *)sum64, fsum);
+  return cudaGetLastError();
+}
+
+}  // namespace gpu
+}  // namespace illumina

@@ -1,0 +1,946 @@
+// Runtime behind the C ABI: the depth model (createDepthModel / DepthModel,
+// src/model/runner.ts:79-485), the stateless shading entry point
+// (src/lighting/renderer.ts + shade.ts + composite.ts), the per-kernel entry
+// points and the synthetic-workload helpers.
+//
+// Model life cycle: create() parses or synthesises the weights, plans and
+// validates the arena exactly as the reference does, uploads the logical
+// weights once and repacks them on the device into the kernels' layouts, and
+// allocates ONE device arena sized for max_batch frames plus the bilateral
+// guide and the depth ping-pong. forward() records the op list (40 launches)
+// into a CUDA graph on first use for a given (n, pointers) and replays it;
+// nothing is allocated per call.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <mutex>
+
+#include "host.h"
+#include "illumina.h"
+#include "kernels.h"
+
+using namespace illumina;
+
+namespace illumina {
+namespace {
+thread_local std::string g_last_error;
+}
+void set_last_error(const std::string &msg) { g_last_error = msg; }
+}  // namespace illumina
+
+#define ILL_TRY try {
+#define ILL_CATCH                                          \
+  }                                                        \
+  catch (const Error &e) {                                 \
+    set_last_error(e.what());                              \
+    return e.status;                                       \
+  }                                                        \
+  catch (const std::bad_alloc &) {                         \
+    set_last_error("out of host memory");                  \
+    return ILLUMINA_INVALID_ARG;                           \
+  }                                                        \
+  catch (const std::exception &e) {                        \
+    set_last_error(e.what());                              \
+    return ILLUMINA_INVALID_ARG;                           \
+  }
+
+namespace {
+
+void cuda_check(cudaError_t e, const char *what) {
+  if (e != cudaSuccess)
+    throw Error(ILLUMINA_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+bool is_device_ptr(const void *p) {
+  if (!p) return false;
+  cudaPointerAttributes at;
+  cudaError_t e = cudaPointerGetAttributes(&at, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct GraphKey {
+  int n, layout, mode;
+  const void *frames, *disp, *low, *hist, *tex;
+  bool operator==(const GraphKey &o) const {
+    return n == o.n && layout == o.layout && mode == o.mode && frames == o.frames && disp == o.disp &&
+           low == o.low && hist == o.hist && tex == o.tex;
+  }
+};
+
+struct OpWeights {
+  const float *w = nullptr, *b = nullptr, *dw_w = nullptr, *dw_b = nullptr;
+  float head_bias = 0.0f;
+};
+
+}  // namespace
+
+struct illumina_model {
+  Architecture arch;
+  ArenaPlan plan;
+  illumina_model_options opts{};
+  int device = 0;
+  int T = gpu::F32;
+  size_t elt = 4;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev_join = nullptr, ev_done = nullptr;
+  std::vector<float> host_weights;  // logical blob (kept for debug / re-pack)
+  float *d_weights_logical = nullptr;
+  float *d_weights = nullptr;
+  std::vector<OpWeights> opw;
+  char *d_arena = nullptr;
+  size_t arena_alloc = 0;
+  std::vector<size_t> buf_off;
+  float *d_luma = nullptr;
+  float *d_scene = nullptr;
+  float *d_tex[2] = {nullptr, nullptr};
+  float *d_stage_in = nullptr, *d_stage_out = nullptr, *d_stage_low = nullptr;
+  size_t device_bytes = 0;
+  int history_index = 0, last_written = 1;
+  float exposure = 1, range_sigma = 0.12f, base_alpha = 0.35f, sensitivity = 3.0f;
+  std::vector<std::pair<GraphKey, cudaGraphExec_t>> graphs;
+  int launches_per_forward = 0;
+
+  void *tensor(const std::string &name) {
+    auto it = plan.assignment.find(name);
+    if (it == plan.assignment.end()) throw Error(ILLUMINA_INVALID_ARG, "runner: " + name + " has no arena buffer");
+    return d_arena + buf_off[it->second];
+  }
+  void clear_graphs() {
+    for (auto &g : graphs) cudaGraphExecDestroy(g.second);
+    graphs.clear();
+  }
+  ~illumina_model();
+};
+
+illumina_model::~illumina_model() {
+  if (device >= 0) cudaSetDevice(device);
+  clear_graphs();
+  cudaFree(d_weights_logical);
+  cudaFree(d_weights);
+  cudaFree(d_arena);
+  cudaFree(d_luma);
+  cudaFree(d_scene);
+  cudaFree(d_tex[0]);
+  cudaFree(d_tex[1]);
+  cudaFree(d_stage_in);
+  cudaFree(d_stage_out);
+  cudaFree(d_stage_low);
+  if (ev_join) cudaEventDestroy(ev_join);
+  if (ev_done) cudaEventDestroy(ev_done);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+namespace {
+
+template <typename F>
+size_t write_json(const std::string &s, char *buf, size_t cap, size_t *needed, F) {
+  if (needed) *needed = s.size() + 1;
+  if (buf && cap > 0) {
+    size_t n = std::min(cap - 1, s.size());
+    std::memcpy(buf, s.data(), n);
+    buf[n] = 0;
+  }
+  return s.size() + 1;
+}
+
+gpu::PreprocessParams preprocess_params(const illumina_model &m) {
+  gpu::PreprocessParams p;
+  for (int i = 0; i < 3; i++) {
+    p.mean[i] = (float)m.arch.mean[i];
+    p.std[i] = (float)m.arch.std[i];
+    p.inv_std[i] = (float)(1.0 / m.arch.std[i]);
+  }
+  p.exposure = m.exposure;
+  p.decode_srgb = m.opts.decode_srgb ? 1 : 0;
+  return p;
+}
+
+// Enqueues the whole op list on m.stream. mode 0: independent frames -> disp;
+// mode 1: streaming frame with history (n == 1).
+int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, float *disp, float *low_out,
+                    const float *history, float *out_tex, const std::vector<cudaEvent_t> *marks = nullptr) {
+  const Architecture &a = m.arch;
+  const int S = a.input_size;
+  int launches = 0;
+  cudaStream_t st = m.stream;
+  for (size_t i = 0; i < a.ops.size(); i++) {
+    const Op &op = a.ops[i];
+    if (marks) cuda_check(cudaEventRecord((*marks)[i], st), "profile event");
+    const OpWeights &w = m.opw[i];
+    switch (op.kind) {
+      case OpKind::Preprocess:
+        cuda_check(gpu::preprocess(m.T, frames, layout, n, S, preprocess_params(m), m.tensor(op.out), m.d_luma,
+                                   m.d_scene, st),
+                   "preprocess");
+        launches++;
+        break;
+      case OpKind::Conv: {
+        const TensorShape &si = a.shape(op.in), &so = a.shape(op.out);
+        cuda_check(gpu::conv(m.T, m.tensor(op.in), n, si.h, si.w, si.c, w.w, w.b, so.c, op.k, op.stride, op.act,
+                             m.tensor(op.out), st),
+                   op.name.c_str());
+        launches++;
+        break;
+      }
+      case OpKind::Pw:
+      case OpKind::Dwpw:
+      case OpKind::Lateral: {
+        const TensorShape &so = a.shape(op.out);
+        gpu::GemmOp g;
+        g.n = n;
+        g.dst = m.tensor(op.out);
+        g.bias = w.b;
+        g.w = w.w;
+        g.N = so.c;
+        g.act = op.act;
+        g.OH = so.h, g.OW = so.w;
+        g.M = (long)n * so.h * so.w;
+        if (op.kind == OpKind::Lateral) {
+          const TensorShape &ss = a.shape(op.skip);
+          g.mode = 2;
+          g.src = m.tensor(op.skip);
+          g.coarse = m.tensor(op.coarse);
+          g.K = ss.c;
+        } else {
+          const TensorShape &si = a.shape(op.in);
+          g.src = m.tensor(op.in);
+          g.K = si.c;
+          g.res = op.residual.empty() ? nullptr : m.tensor(op.residual);
+          if (op.kind == OpKind::Dwpw) {
+            g.mode = 1;
+            g.H = si.h, g.W = si.w;
+            g.ks = op.k, g.stride = op.stride;
+            g.mid_act = op.mid_act;
+            g.dw_w = w.dw_w, g.dw_b = w.dw_b;
+          } else {
+            g.mode = 0;
+          }
+        }
+        cuda_check(gpu::gemm(m.T, g, st), op.name.c_str());
+        launches++;
+        break;
+      }
+      case OpKind::Head: {
+        const TensorShape &si = a.shape(op.in);
+        long M = (long)n * si.h * si.w;
+        float *low = (float *)m.tensor(op.out);
+        cuda_check(gpu::head(m.T, m.tensor(op.in), M, si.c, w.w, w.head_bias, low, nullptr, st), "head");
+        launches++;
+        if (low_out) {
+          cuda_check(cudaMemcpyAsync(low_out, low, sizeof(float) * M, cudaMemcpyDeviceToDevice, st), "depth_low copy");
+        }
+        break;
+      }
+      case OpKind::BilateralUp: {
+        const TensorShape &si = a.shape(op.in);
+        gpu::BilateralParams bp{m.range_sigma, m.base_alpha, m.sensitivity};
+        cuda_check(gpu::bilateral((const float *)m.tensor(op.in), n, si.h, si.w, m.d_luma, bp, disp, history,
+                                  out_tex, st),
+                   "bilateralUp");
+        launches++;
+        break;
+      }
+    }
+  }
+  if (marks) cuda_check(cudaEventRecord((*marks)[a.ops.size()], st), "profile event");
+  return launches;
+}
+
+cudaGraphExec_t graph_for(illumina_model &m, const GraphKey &key, const float *frames, float *disp, float *low,
+                          const float *hist, float *tex) {
+  for (auto &g : m.graphs)
+    if (g.first == key) return g.second;
+  if (m.graphs.size() >= 8) {
+    cudaGraphExecDestroy(m.graphs.front().second);
+    m.graphs.erase(m.graphs.begin());
+  }
+  cuda_check(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+  int launches = 0;
+  try {
+    launches = enqueue_forward(m, key.n, frames, key.layout, disp, low, hist, tex);
+  } catch (...) {
+    cudaGraph_t g = nullptr;
+    cudaStreamEndCapture(m.stream, &g);
+    if (g) cudaGraphDestroy(g);
+    throw;
+  }
+  cudaGraph_t graph = nullptr;
+  cuda_check(cudaStreamEndCapture(m.stream, &graph), "end capture");
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  cuda_check(e, "graph instantiate");
+  m.launches_per_forward = launches;
+  m.graphs.push_back({key, exec});
+  return exec;
+}
+
+// Runs the hot path with caller pointers (host or device). Host pointers are
+// staged through the model's device buffers and make the call synchronous.
+void run_forward(illumina_model &m, const float *frames, int n, int layout, float *disp, float *low,
+                 cudaStream_t caller, int mode) {
+  if (n < 1 || n > m.opts.max_batch)
+    throw Error(ILLUMINA_INVALID_ARG, "forward: batch " + std::to_string(n) + " outside [1, " +
+                                          std::to_string(m.opts.max_batch) + "]");
+  if (layout != ILLUMINA_FRAME_RGB_PLANAR && layout != ILLUMINA_FRAME_RGBA_INTERLEAVED)
+    throw Error(ILLUMINA_INVALID_ARG, "forward: unknown frame layout " + std::to_string(layout));
+  if (!frames) throw Error(ILLUMINA_INVALID_ARG, "forward: frames is null");
+  cuda_check(cudaSetDevice(m.device), "cudaSetDevice");
+  const int S = m.arch.input_size;
+  const long frame_floats = (layout == ILLUMINA_FRAME_RGB_PLANAR ? 3L : 4L) * S * S;
+  const long disp_floats = (long)S * S, low_floats = (long)(S / 2) * (S / 2);
+  bool host_in = !is_device_ptr(frames);
+  bool host_disp = disp && !is_device_ptr(disp);
+  bool host_low = low && !is_device_ptr(low);
+  bool sync = host_in || host_disp || host_low;
+
+  cuda_check(cudaEventRecord(m.ev_join, caller), "event record");
+  cuda_check(cudaStreamWaitEvent(m.stream, m.ev_join, 0), "stream wait");
+
+  const float *f_dev = frames;
+  if (host_in) {
+    size_t bytes = sizeof(float) * n * frame_floats;
+    cuda_check(cudaMemcpyAsync(m.d_stage_in, frames, bytes, cudaMemcpyHostToDevice, m.stream), "frames H2D");
+    f_dev = m.d_stage_in;
+  }
+  float *d_disp = host_disp ? m.d_stage_out : disp;
+  float *d_low = host_low ? m.d_stage_low : low;
+  if (!d_disp && mode == 0) d_disp = m.d_stage_out;
+
+  const float *hist = nullptr;
+  float *tex = nullptr;
+  if (mode == 1) {
+    m.last_written = 1 - m.history_index;
+    hist = m.d_tex[m.history_index];
+    tex = m.d_tex[1 - m.history_index];
+  }
+  GraphKey key{n, layout, mode, f_dev, d_disp, d_low, hist, tex};
+  cudaGraphExec_t exec = graph_for(m, key, f_dev, d_disp, d_low, hist, tex);
+  cuda_check(cudaGraphLaunch(exec, m.stream), "graph launch");
+
+  if (host_disp)
+    cuda_check(cudaMemcpyAsync(disp, m.d_stage_out, sizeof(float) * n * disp_floats, cudaMemcpyDeviceToHost, m.stream),
+               "disparity D2H");
+  if (host_low)
+    cuda_check(cudaMemcpyAsync(low, m.d_stage_low, sizeof(float) * n * low_floats, cudaMemcpyDeviceToHost, m.stream),
+               "depth_low D2H");
+  cuda_check(cudaEventRecord(m.ev_done, m.stream), "event record");
+  cuda_check(cudaStreamWaitEvent(caller, m.ev_done, 0), "caller wait");
+  if (sync) cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+}
+
+void build_model(illumina_model &m, const illumina_model_options &o) {
+  m.opts = o;
+  if (m.opts.max_batch < 1) throw Error(ILLUMINA_INVALID_ARG, "createDepthModel: max_batch must be >= 1");
+  if (o.precision != ILLUMINA_PRECISION_F32 && o.precision != ILLUMINA_PRECISION_BF16)
+    throw Error(ILLUMINA_INVALID_ARG, "createDepthModel: unknown precision " + std::to_string(o.precision));
+  m.arch = build_architecture(o.input_size);
+  m.T = o.precision == ILLUMINA_PRECISION_BF16 ? gpu::BF16 : gpu::F32;
+  m.elt = m.T == gpu::BF16 ? 2 : 4;
+  m.exposure = o.exposure;
+  m.range_sigma = o.range_sigma;
+  m.base_alpha = o.temporal_base;
+  m.sensitivity = o.temporal_sensitivity;
+
+  // --- weights (host) ---
+  size_t count = weight_count(m.arch);
+  if (o.weights && o.weights_count) {
+    if (o.weights_count != count)
+      throw Error(ILLUMINA_BAD_WEIGHTS, "weights: blob has " + std::to_string(o.weights_count) + " values, expected " +
+                                            std::to_string(count));
+    m.host_weights.assign(o.weights, o.weights + count);
+  } else if (o.idm_bytes && o.idm_len) {
+    m.host_weights = parse_weights(m.arch, (const uint8_t *)o.idm_bytes, o.idm_len);
+  } else if (o.idm_path && o.idm_path[0]) {
+    std::ifstream f(o.idm_path, std::ios::binary);
+    if (!f) throw Error(ILLUMINA_BAD_WEIGHTS, std::string("weights: cannot open ") + o.idm_path);
+    std::vector<uint8_t> bytes((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    m.host_weights = parse_weights(m.arch, bytes.data(), bytes.size());
+  } else {
+    m.host_weights = synthesize_weights(m.arch, o.synth_seed);
+  }
+
+  // --- arena plan (runner.ts:190-192) ---
+  std::vector<std::string> exclude = {"depth"};
+  m.plan = plan_arena(m.arch, exclude, o.keep_intermediates != 0);
+  validate_arena(m.arch, m.plan, exclude);
+
+  // --- device ---
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    throw Error(ILLUMINA_NO_DEVICE, "createDepthModel: no CUDA device");
+  }
+  if (o.device < 0 || o.device >= ndev)
+    throw Error(ILLUMINA_INVALID_ARG, "createDepthModel: device " + std::to_string(o.device) + " out of range");
+  m.device = o.device;
+  cuda_check(cudaSetDevice(m.device), "cudaSetDevice");
+  cuda_check(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking), "stream create");
+  cuda_check(cudaEventCreateWithFlags(&m.ev_join, cudaEventDisableTiming), "event create");
+  cuda_check(cudaEventCreateWithFlags(&m.ev_done, cudaEventDisableTiming), "event create");
+
+  // Upload the logical blob, then repack per op on the device.
+  cuda_check(cudaMalloc(&m.d_weights_logical, count * 4), "cudaMalloc weights");
+  cuda_check(cudaMemcpy(m.d_weights_logical, m.host_weights.data(), count * 4, cudaMemcpyHostToDevice), "weights H2D");
+  auto specs = weight_specs(m.arch);
+  std::map<std::string, const WeightSpec *> by_name;
+  for (const auto &s : specs) by_name[s.name] = &s;
+  // packed buffer: same element count, each tensor 16-byte aligned
+  std::vector<size_t> pk_off(specs.size());
+  size_t total = 0;
+  for (size_t i = 0; i < specs.size(); i++) {
+    pk_off[i] = total;
+    total = align_up(total + specs[i].count, 4);
+  }
+  cuda_check(cudaMalloc(&m.d_weights, total * 4), "cudaMalloc packed weights");
+  m.device_bytes += (count + total) * 4;
+  int rb = m.T == gpu::BF16 ? 1 : 0;
+  std::map<std::string, float *> packed;
+  for (size_t i = 0; i < specs.size(); i++) {
+    const auto &s = specs[i];
+    const float *src = m.d_weights_logical + s.offset;
+    float *dst = m.d_weights + pk_off[i];
+    bool bias = s.name.size() >= 4 && s.name.compare(s.name.size() - 4, 4, "bias") == 0;
+    if (s.name.find("dw_weight") != std::string::npos)
+      cuda_check(gpu::pack_dw(src, s.shape[0], s.shape[1], dst, rb, m.stream), "pack dw");
+    else if (s.shape.size() == 4)
+      cuda_check(gpu::pack_conv(src, s.shape[0], s.shape[1], s.shape[2], dst, rb, m.stream), "pack conv");
+    else
+      cuda_check(gpu::copy_round(src, (long)s.count, dst, bias ? 0 : rb, m.stream), "pack");
+    packed[s.name] = dst;
+  }
+  m.opw.resize(m.arch.ops.size());
+  for (size_t i = 0; i < m.arch.ops.size(); i++) {
+    const Op &op = m.arch.ops[i];
+    OpWeights &w = m.opw[i];
+    auto get = [&](const std::string &suffix) -> float * {
+      auto it = packed.find(op.name + "." + suffix);
+      if (it == packed.end()) throw Error(ILLUMINA_BAD_WEIGHTS, "weights: " + op.name + "." + suffix + " is missing");
+      return it->second;
+    };
+    switch (op.kind) {
+      case OpKind::Conv:
+      case OpKind::Pw:
+      case OpKind::Lateral:
+      case OpKind::Head:
+        w.w = get("weight");
+        w.b = get("bias");
+        break;
+      case OpKind::Dwpw:
+        w.dw_w = get("dw_weight");
+        w.dw_b = get("dw_bias");
+        w.w = get("pw_weight");
+        w.b = get("pw_bias");
+        break;
+      default: break;
+    }
+    if (op.kind == OpKind::Head) w.head_bias = m.host_weights[by_name[op.name + ".bias"]->offset];
+  }
+
+  // --- arena: one allocation, buffers 256-byte aligned, sized for max_batch ---
+  const size_t B = (size_t)m.opts.max_batch;
+  m.buf_off.resize(m.plan.buffer_sizes.size());
+  size_t off = 0;
+  for (size_t b = 0; b < m.plan.buffer_sizes.size(); b++) {
+    m.buf_off[b] = off;
+    off = align_up(off + (size_t)m.plan.buffer_sizes[b] * 4 * m.elt * B, 256);
+  }
+  m.arena_alloc = off;
+  cuda_check(cudaMalloc(&m.d_arena, off), "cudaMalloc arena");
+  const int S = m.arch.input_size;
+  cuda_check(cudaMalloc(&m.d_luma, sizeof(float) * B * S * S), "cudaMalloc guide");
+  if (o.keep_intermediates) cuda_check(cudaMalloc(&m.d_scene, sizeof(float) * 4 * B * S * S), "cudaMalloc scene");
+  for (int i = 0; i < 2; i++) {
+    cuda_check(cudaMalloc(&m.d_tex[i], sizeof(float) * 4 * S * S), "cudaMalloc depth");
+    cuda_check(cudaMemsetAsync(m.d_tex[i], 0, sizeof(float) * 4 * S * S, m.stream), "clear depth");
+  }
+  cuda_check(cudaMalloc(&m.d_stage_in, sizeof(float) * 4 * B * S * S), "cudaMalloc staging");
+  cuda_check(cudaMalloc(&m.d_stage_out, sizeof(float) * B * S * S), "cudaMalloc staging");
+  cuda_check(cudaMalloc(&m.d_stage_low, sizeof(float) * B * (S / 2) * (S / 2)), "cudaMalloc staging");
+  m.device_bytes += off + sizeof(float) * B * S * S * (1 + 4 + 1) + sizeof(float) * B * (S / 2) * (S / 2) +
+                    2 * sizeof(float) * 4 * S * S + (m.d_scene ? sizeof(float) * 4 * B * S * S : 0);
+  cuda_check(cudaStreamSynchronize(m.stream), "create synchronize");
+  // The logical copy is only needed for packing.
+  cudaFree(m.d_weights_logical);
+  m.d_weights_logical = nullptr;
+  m.device_bytes -= count * 4;
+  m.launches_per_forward = (int)m.arch.ops.size();
+}
+
+// Op-API helper: temporary device scratch on a stream.
+struct Scratch {
+  void *p = nullptr;
+  cudaStream_t st;
+  Scratch(size_t bytes, cudaStream_t s) : st(s) { cuda_check(cudaMallocAsync(&p, bytes, s), "cudaMallocAsync"); }
+  ~Scratch() {
+    if (p) cudaFreeAsync(p, st);
+  }
+};
+
+void require(bool ok, const std::string &msg) {
+  if (!ok) throw Error(ILLUMINA_INVALID_ARG, msg);
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+
+extern "C" {
+
+const char *illumina_last_error(void) { return g_last_error.c_str(); }
+const char *illumina_version(void) { return "illumina-b200 0.1 (sm_100a)"; }
+
+int illumina_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+illumina_status illumina_arch_json(int input_size, char *buf, size_t cap, size_t *needed) {
+  ILL_TRY
+  write_json(arch_to_json(build_architecture(input_size)), buf, cap, needed, 0);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_arena_json(int input_size, char *buf, size_t cap, size_t *needed) {
+  ILL_TRY
+  Architecture a = build_architecture(input_size);
+  std::vector<std::string> ex = {"depth"};
+  ArenaPlan p = plan_arena(a, ex);
+  validate_arena(a, p, ex);
+  write_json(arena_to_json(p), buf, cap, needed, 0);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_weights_count(int input_size, size_t *count) {
+  ILL_TRY
+  require(count != nullptr, "weights_count: count is null");
+  *count = weight_count(build_architecture(input_size));
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_weights_synthesize(int input_size, uint32_t seed, float *out, size_t count) {
+  ILL_TRY
+  Architecture a = build_architecture(input_size);
+  require(out && count == weight_count(a), "synthesizeWeights: output must hold " + std::to_string(weight_count(a)) + " floats");
+  auto blob = synthesize_weights(a, seed);
+  std::memcpy(out, blob.data(), blob.size() * 4);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_weights_parse(int input_size, const void *bytes, size_t len, float *out, size_t count) {
+  ILL_TRY
+  Architecture a = build_architecture(input_size);
+  require(out && count == weight_count(a), "parseWeights: output must hold " + std::to_string(weight_count(a)) + " floats");
+  require(bytes != nullptr || len == 0, "parseWeights: bytes is null");
+  auto blob = parse_weights(a, (const uint8_t *)bytes, len);
+  std::memcpy(out, blob.data(), blob.size() * 4);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_weights_serialize(int input_size, const float *blob, size_t count, void *out, size_t cap,
+                                           size_t *needed) {
+  ILL_TRY
+  Architecture a = build_architecture(input_size);
+  require(blob != nullptr, "serializeWeights: blob is null");
+  auto bytes = serialize_weights(a, blob, count);
+  if (needed) *needed = bytes.size();
+  if (out) {
+    require(cap >= bytes.size(), "serializeWeights: output buffer too small");
+    std::memcpy(out, bytes.data(), bytes.size());
+  }
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+double illumina_half_to_float(uint16_t h) { return half_to_float(h); }
+
+void illumina_model_options_default(illumina_model_options *o) {
+  if (!o) return;
+  std::memset(o, 0, sizeof *o);
+  o->input_size = 448;
+  o->device = 0;
+  o->max_batch = 1;
+  o->precision = ILLUMINA_PRECISION_F32;
+  o->decode_srgb = 1;
+  o->exposure = 1.0f;
+  o->range_sigma = 0.12f;
+  o->temporal_base = 0.35f;
+  o->temporal_sensitivity = 3.0f;
+  o->synth_seed = 1;
+}
+
+illumina_status illumina_model_create(const illumina_model_options *opts, illumina_model **out) {
+  ILL_TRY
+  require(opts && out, "createDepthModel: null argument");
+  *out = nullptr;
+  auto m = std::make_unique<illumina_model>();
+  m->device = -1;
+  build_model(*m, *opts);
+  *out = m.release();
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_destroy(illumina_model *model) {
+  delete model;
+  return ILLUMINA_OK;
+}
+
+illumina_status illumina_model_set_exposure(illumina_model *m, float exposure) {
+  ILL_TRY
+  require(m, "setExposure: null model");
+  if (m->exposure != exposure) m->clear_graphs();
+  m->exposure = exposure;
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_set_temporal(illumina_model *m, float base, float sens, float sigma) {
+  ILL_TRY
+  require(m, "setTemporal: null model");
+  if (m->base_alpha != base || m->sensitivity != sens || m->range_sigma != sigma) m->clear_graphs();
+  m->base_alpha = base, m->sensitivity = sens, m->range_sigma = sigma;
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_forward(illumina_model *m, const float *frames, int n, int layout, float *disparity,
+                                 float *depth_low, void *stream) {
+  ILL_TRY
+  require(m, "forward: null model");
+  run_forward(*m, frames, n, layout, disparity, depth_low, (cudaStream_t)stream, 0);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_record(illumina_model *m, const float *frame, int layout, void *stream) {
+  ILL_TRY
+  require(m, "record: null model");
+  run_forward(*m, frame, 1, layout, nullptr, nullptr, (cudaStream_t)stream, 1);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_swap_history(illumina_model *m) {
+  ILL_TRY
+  require(m, "swapHistory: null model");
+  m->history_index = 1 - m->history_index;
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+int illumina_model_output_parity(const illumina_model *m) { return m ? 1 - m->history_index : -1; }
+int illumina_model_fresh_parity(const illumina_model *m) { return m ? m->last_written : -1; }
+
+illumina_status illumina_model_depth_slot(illumina_model *m, int index, const float **ptr) {
+  ILL_TRY
+  require(m && ptr, "debugDepth: null argument");
+  *ptr = m->d_tex[index == 0 ? 0 : 1];
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_debug_tensor(illumina_model *m, const char *name, float *out, size_t cap, int *h,
+                                            int *w, int *c, int *live_at_end) {
+  ILL_TRY
+  require(m && name, "debugTensor: null argument");
+  std::string n(name);
+  auto ts = m->arch.tensors.find(n);
+  auto as = m->plan.assignment.find(n);
+  if (ts == m->arch.tensors.end() || as == m->plan.assignment.end())
+    throw Error(ILLUMINA_INVALID_ARG, "debugTensor: unknown tensor " + n);
+  const TensorShape &s = ts->second;
+  if (h) *h = s.h;
+  if (w) *w = s.w;
+  if (c) *c = s.c;
+  // runner.ts:466-476: stolen if any later op writes the same buffer.
+  int produced = -1;
+  for (size_t i = 0; i < m->arch.ops.size(); i++)
+    if (m->arch.ops[i].out == n) {
+      produced = (int)i;
+      break;
+    }
+  bool stolen = false;
+  for (size_t i = 0; i < m->arch.ops.size(); i++) {
+    if ((int)i <= produced) continue;
+    auto o = m->plan.assignment.find(m->arch.ops[i].out);
+    if (o != m->plan.assignment.end() && o->second == as->second) stolen = true;
+  }
+  if (live_at_end) *live_at_end = stolen ? 0 : 1;
+  if (!out) return ILLUMINA_OK;
+  cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+  long count = s.elems();
+  require(cap >= (size_t)count, "debugTensor: output holds " + std::to_string(cap) + " floats, tensor needs " +
+                                    std::to_string(count));
+  float *tmp = nullptr;
+  cuda_check(cudaMalloc(&tmp, sizeof(float) * count), "cudaMalloc");
+  cudaError_t e;
+  if (n == "depth_low") e = gpu::expand4((const float *)m->tensor(n), (long)s.h * s.w, tmp, m->stream);
+  else e = gpu::to_f32(m->T, m->tensor(n), count, tmp, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, tmp, sizeof(float) * count, cudaMemcpyDefault, m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  cudaFree(tmp);
+  cuda_check(e, "debugTensor copy");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_stats(const illumina_model *m, illumina_stats *out) {
+  ILL_TRY
+  require(m && out, "stats: null argument");
+  out->dispatches = (int)m->arch.ops.size();
+  out->launches = m->launches_per_forward;
+  out->arena_bytes = (size_t)m->plan.total_bytes;
+  out->naive_arena_bytes = (size_t)m->plan.naive_bytes;
+  out->weight_bytes = m->host_weights.size() * 4;
+  out->device_bytes = m->device_bytes;
+  out->max_batch = m->opts.max_batch;
+  out->precision = m->opts.precision;
+  out->input_size = m->arch.input_size;
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_profile(illumina_model *m, const float *frames, int n, int layout, int reps,
+                                       float *op_ms, int cap) {
+  ILL_TRY
+  require(m && frames && op_ms, "profile: null argument");
+  require(n >= 1 && n <= m->opts.max_batch, "profile: batch outside [1, max_batch]");
+  require(reps >= 1, "profile: reps must be positive");
+  require(is_device_ptr(frames), "profile: frames must be device memory");
+  const size_t nops = m->arch.ops.size();
+  require(cap >= (int)nops, "profile: op_ms must hold " + std::to_string(nops) + " floats");
+  cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+  std::vector<cudaEvent_t> ev(nops + 1);
+  for (auto &e : ev) cuda_check(cudaEventCreate(&e), "event create");
+  std::vector<double> acc(nops, 0.0);
+  cudaError_t err = cudaSuccess;
+  try {
+    for (int r = 0; r < reps; r++) {
+      enqueue_forward(*m, n, frames, layout, m->d_stage_out, nullptr, nullptr, nullptr, &ev);
+      cuda_check(cudaEventSynchronize(ev[nops]), "profile sync");
+      for (size_t i = 0; i < nops; i++) {
+        float ms = 0;
+        cuda_check(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "elapsed");
+        acc[i] += ms;
+      }
+    }
+  } catch (...) {
+    for (auto &e : ev) cudaEventDestroy(e);
+    throw;
+  }
+  for (auto &e : ev) cudaEventDestroy(e);
+  cuda_check(err, "profile");
+  for (size_t i = 0; i < nops; i++) op_ms[i] = (float)(acc[i] / reps);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+// ---- per-kernel entry points -------------------------------------------------
+
+illumina_status illumina_op_pointwise(const float *src, long pixels, int in_c, const float *w, const float *b,
+                                      int out_c, int act, const float *res, float *dst, void *stream) {
+  ILL_TRY
+  require(src && w && b && dst, "pointwise: null pointer");
+  require(in_c > 0 && out_c > 0 && in_c % 4 == 0 && out_c % 4 == 0, "pointwise: channels must be multiples of 4");
+  require(act >= 0 && act <= 3, "pointwise: unknown activation");
+  gpu::GemmOp g;
+  g.mode = 0, g.src = src, g.w = w, g.bias = b, g.res = res, g.dst = dst, g.M = pixels, g.N = out_c, g.K = in_c;
+  g.act = act;
+  cuda_check(gpu::gemm(gpu::F32, g, (cudaStream_t)stream), "pointwise");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_op_dwpw(const float *src, int in_h, int in_w, int in_c, const float *dw_w, const float *dw_b,
+                                 int mid_act, const float *pw_w, const float *pw_b, int out_c, int k, int stride,
+                                 int act, const float *res, float *dst, void *stream) {
+  ILL_TRY
+  require(src && dw_w && dw_b && pw_w && pw_b && dst, "dwpw: null pointer");
+  require(in_c % 4 == 0 && out_c % 4 == 0 && in_c > 0 && out_c > 0, "dwpw: channels must be multiples of 4");
+  require(k == 3 || k == 5, "dwpw: kernel size must be 3 or 5");
+  require(stride == 1 || stride == 2, "dwpw: stride must be 1 or 2");
+  require(act >= 0 && act <= 3 && mid_act >= 0 && mid_act <= 3, "dwpw: unknown activation");
+  cudaStream_t st = (cudaStream_t)stream;
+  int pad = (k - 1) >> 1;
+  int oh = (in_h + 2 * pad - k) / stride + 1, ow = (in_w + 2 * pad - k) / stride + 1;
+  Scratch pk(sizeof(float) * in_c * k * k, st);
+  cuda_check(gpu::pack_dw(dw_w, in_c, k, (float *)pk.p, 0, st), "pack dw");
+  gpu::GemmOp g;
+  g.mode = 1, g.src = src, g.w = pw_w, g.bias = pw_b, g.res = res, g.dst = dst;
+  g.H = in_h, g.W = in_w, g.OH = oh, g.OW = ow, g.M = (long)oh * ow, g.N = out_c, g.K = in_c;
+  g.act = act, g.mid_act = mid_act, g.ks = k, g.stride = stride, g.dw_w = (const float *)pk.p, g.dw_b = dw_b;
+  cuda_check(gpu::gemm(gpu::F32, g, st), "dwpw");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_op_conv(const float *src, int in_h, int in_w, int in_c, const float *w, const float *b,
+                                 int out_c, int k, int stride, int act, float *dst, void *stream) {
+  ILL_TRY
+  require(src && w && b && dst, "conv: null pointer");
+  require(in_c % 4 == 0 && out_c % 4 == 0 && in_c > 0 && out_c > 0, "conv: channels must be multiples of 4");
+  require(k >= 1 && k % 2 == 1 && stride >= 1, "conv: odd kernel size and positive stride required");
+  require(act >= 0 && act <= 3, "conv: unknown activation");
+  cudaStream_t st = (cudaStream_t)stream;
+  Scratch pk(sizeof(float) * out_c * in_c * k * k, st);
+  cuda_check(gpu::pack_conv(w, out_c, in_c, k, (float *)pk.p, 0, st), "pack conv");
+  cuda_check(gpu::conv(gpu::F32, src, 1, in_h, in_w, in_c, (const float *)pk.p, b, out_c, k, stride, act, dst, st),
+             "conv");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_op_lateral(const float *coarse, int ch, int cw, const float *skip, int skip_c, const float *w,
+                                    const float *b, int out_c, int act, float *dst, void *stream) {
+  ILL_TRY
+  require(coarse && skip && w && b && dst, "lateral: null pointer");
+  require(skip_c % 4 == 0 && out_c % 4 == 0 && skip_c > 0 && out_c > 0, "lateral: channels must be multiples of 4");
+  require(act >= 0 && act <= 3, "lateral: unknown activation");
+  gpu::GemmOp g;
+  g.mode = 2, g.src = skip, g.coarse = coarse, g.w = w, g.bias = b, g.dst = dst;
+  g.OH = 2 * ch, g.OW = 2 * cw, g.M = 4L * ch * cw, g.N = out_c, g.K = skip_c, g.act = act;
+  cuda_check(gpu::gemm(gpu::F32, g, (cudaStream_t)stream), "lateral");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_op_head(const float *src, long pixels, int in_c, const float *w, float b, float *dst4,
+                                 void *stream) {
+  ILL_TRY
+  require(src && w && dst4, "head: null pointer");
+  require(in_c % 4 == 0 && in_c > 0, "head: channels must be a multiple of 4");
+  cuda_check(gpu::head(gpu::F32, src, pixels, in_c, w, b, nullptr, dst4, (cudaStream_t)stream), "head");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_op_preprocess(const float *frames, int n, int layout, int size, int decode_srgb,
+                                       float exposure, float *input, float *scene_color, void *stream) {
+  ILL_TRY
+  require(frames && input, "preprocess: null pointer");
+  require(layout == 0 || layout == 1, "preprocess: unknown layout");
+  gpu::PreprocessParams p;
+  const double mean[3] = {0.485, 0.456, 0.406}, stdv[3] = {0.229, 0.224, 0.225};
+  for (int i = 0; i < 3; i++) p.mean[i] = (float)mean[i], p.std[i] = (float)stdv[i], p.inv_std[i] = (float)(1 / stdv[i]);
+  p.exposure = exposure;
+  p.decode_srgb = decode_srgb ? 1 : 0;
+  cuda_check(gpu::preprocess(gpu::F32, frames, layout, n, size, p, input, nullptr, scene_color, (cudaStream_t)stream),
+             "preprocess");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_op_bilateral(const float *low, int lh, int lw, int low_c, const float *guide, int guide_c,
+                                      float range_sigma, float *dst, void *stream) {
+  ILL_TRY
+  require(low && guide && dst, "bilateral: null pointer");
+  require(lh > 0 && lw > 0 && low_c >= 1 && guide_c >= 3, "bilateral: bad shape");
+  cuda_check(gpu::bilateral_strided(low, lh, lw, low_c, guide, guide_c, range_sigma, dst, (cudaStream_t)stream),
+             "bilateral");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+// ---- lighting ------------------------------------------------------------------
+
+void illumina_shading_settings_default(illumina_shading_settings *s) {
+  if (!s) return;
+  std::memset(s, 0, sizeof *s);
+  s->fov_y = (float)(58.0 * M_PI / 180.0);
+  s->near_m = 0.35f, s->far_m = 14.0f;
+  s->ao_strength = 0.85f, s->shadow_strength = 0.8f, s->volumetric = 0.35f, s->exposure = 1.15f;
+  s->ambient[0] = 0.16f, s->ambient[1] = 0.2f, s->ambient[2] = 0.3f;
+  s->ambient_intensity = 0.5f, s->roughness = 0.55f, s->fog_density = 0.028f;
+  s->fog_color[0] = 0.05f, s->fog_color[1] = 0.07f, s->fog_color[2] = 0.12f;
+  s->specular = 0.6f, s->normal_strength = 1.0f, s->albedo_mix = 1.0f, s->contact_shadow_length = 0.8f;
+  s->ao_radius_pixels = 14.0f;
+  s->tone_map = 0;
+  s->contrast = 1.04f, s->saturation = 1.06f, s->vignette = 0.35f;
+  s->debug_view = 0;
+}
+
+illumina_status illumina_shade(const float *disparity, int dw, int dh, int dch, const float *albedo, int aw, int ah,
+                               const illumina_light *lights, const illumina_shading_settings *s, uint32_t frame,
+                               const illumina_shade_steps *steps, int out_w, int out_h, float *hdr, uint8_t *rgba8,
+                               void *stream) {
+  ILL_TRY
+  require(disparity && albedo && lights && s, "shade: null pointer");
+  require(dw > 0 && dh > 0 && aw > 0 && ah > 0 && out_w > 0 && out_h > 0, "shade: sizes must be positive");
+  require(dch == 1 || dch == 4, "shade: disparity_channels must be 1 or 4");
+  require(s->debug_view >= 0 && s->debug_view <= 4, "shade: unknown debug view");
+  // Renderer.update (renderer.ts:206-231)
+  gpu::ShadeParams P;
+  float cam[4] = {std::tan(s->fov_y / 2), (float)out_w / (float)out_h, s->near_m, s->far_m};
+  float tog[4] = {s->ao_strength, s->shadow_strength, s->volumetric, s->exposure};
+  float amb[4] = {s->ambient[0], s->ambient[1], s->ambient[2], s->ambient_intensity};
+  float misc[4] = {(float)(frame % 4096), s->roughness, s->fog_density, s->normal_strength};
+  float fog[4] = {s->fog_color[0], s->fog_color[1], s->fog_color[2], s->specular};
+  float size[4] = {(float)out_w, (float)out_h, (float)dw, (float)dh};
+  float dbg[4] = {(float)s->debug_view, s->albedo_mix, s->contact_shadow_length, s->ao_radius_pixels};
+  float grade[4] = {(float)(s->tone_map == 0 ? 0 : 1), s->contrast, s->saturation, s->vignette};
+  std::memcpy(P.camera, cam, 16), std::memcpy(P.toggles, tog, 16), std::memcpy(P.ambient, amb, 16);
+  std::memcpy(P.misc, misc, 16), std::memcpy(P.fog, fog, 16), std::memcpy(P.size, size, 16);
+  std::memcpy(P.debug, dbg, 16), std::memcpy(P.grade, grade, 16);
+  gpu::ShadeSteps st{12, 6, 4, 10};
+  if (steps) {
+    require(steps->contact > 0 && steps->ao_dirs > 0 && steps->ao_steps > 0 && steps->volumetric > 0,
+            "shade: step counts must be positive");
+    st = gpu::ShadeSteps{steps->contact, steps->ao_dirs, steps->ao_steps, steps->volumetric};
+  }
+  gpu::ShadeLight L[8];
+  std::memcpy(L, lights, sizeof(L));
+  cuda_check(gpu::shade(disparity, dw, dh, dch, albedo, aw, ah, L, P, st, out_w, out_h, hdr, rgba8, (cudaStream_t)stream),
+             "shade");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh, void *stream) {
+  ILL_TRY
+  require(src && dst && sw > 0 && sh > 0 && dw > 0 && dh > 0, "resize: bad arguments");
+  cuda_check(gpu::resize_bilinear(src, sw, sh, dst, dw, dh, (cudaStream_t)stream), "resize");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+// ---- workloads -------------------------------------------------------------------
+
+illumina_status illumina_generate_frames(int kind, uint32_t seed0, int n, int size, float *out, void *stream) {
+  ILL_TRY
+  require(out && n >= 0 && size > 0, "generate_frames: bad arguments");
+  require(kind == ILLUMINA_FRAMES_UNIFORM || kind == ILLUMINA_FRAMES_BLOBS, "generate_frames: unknown kind");
+  cuda_check(gpu::generate_frames(kind, seed0, n, size, out, (cudaStream_t)stream), "generate_frames");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_checksums(const float *maps, int n, long count, uint64_t *sum64, double *fsum, void *stream) {
+  ILL_TRY
+  require(maps && sum64 && fsum && n >= 0 && count > 0, "checksums: bad arguments");
+  cuda_check(gpu::checksums(maps, n, count, sum64, fsum, (cudaStream_t)stream), "checksums");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+}  // extern "C"

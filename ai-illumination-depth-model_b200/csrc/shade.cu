@@ -1,0 +1,372 @@
+// Depth-aware shading + tone-map in one sm_100a kernel.
+//
+// Per render pixel (src/lighting/shade.ts:312-528): nearest disparity fetch,
+// reciprocal depth map (:81-89), unprojection (:103-111), "accurate" normal
+// reconstruction from a 5-tap cross (:135-169), bilinear sRGB albedo
+// (renderer.ts:127-132), horizon AO (:242-274), up to 8 lights with windowed
+// inverse-square / spot cones (:392-420), screen-space contact shadows
+// (:202-230), GGX D x Smith-Schlick G specular (:287-308), volumetric
+// in-scattering along the view ray (:452-488), depth fog (:496-501), exposure
+// and the debug views (:506-517). The composite pass (composite.ts:87-113:
+// ACES / Reinhard, saturation, contrast, vignette, exact linear->sRGB) is
+// fused as the epilogue, writing 8-bit RGBA directly: the HDR target is
+// optional.
+//
+// The depth map (448x448 float32 = 0.8 MB) stays resident in L2/L1 for the
+// ~90 dependent fetches per pixel; every fetch goes through the read-only
+// path. Step counts are runtime parameters so the reference constants and
+// longer marches share one kernel.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+
+namespace illumina {
+namespace gpu {
+
+namespace {
+
+struct v3 {
+  float x, y, z;
+};
+__device__ __forceinline__ v3 mk(float x, float y, float z) { return v3{x, y, z}; }
+__device__ __forceinline__ v3 operator+(v3 a, v3 b) { return mk(a.x + b.x, a.y + b.y, a.z + b.z); }
+__device__ __forceinline__ v3 operator-(v3 a, v3 b) { return mk(a.x - b.x, a.y - b.y, a.z - b.z); }
+__device__ __forceinline__ v3 operator*(float s, v3 a) { return mk(s * a.x, s * a.y, s * a.z); }
+__device__ __forceinline__ v3 mulv(v3 a, v3 b) { return mk(a.x * b.x, a.y * b.y, a.z * b.z); }
+__device__ __forceinline__ v3 divs(v3 a, float s) { return mk(a.x / s, a.y / s, a.z / s); }
+__device__ __forceinline__ float dot3(v3 a, v3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+__device__ __forceinline__ float len3(v3 a) { return sqrtf(dot3(a, a)); }
+__device__ __forceinline__ v3 norm3(v3 a) { return divs(a, len3(a)); }
+__device__ __forceinline__ v3 cross3(v3 a, v3 b) {
+  return mk(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);
+}
+__device__ __forceinline__ float clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); }
+__device__ __forceinline__ float mixf(float a, float b, float t) { return a * (1.0f - t) + b * t; }
+__device__ __forceinline__ v3 mixv(v3 a, v3 b, float t) {
+  return mk(mixf(a.x, b.x, t), mixf(a.y, b.y, t), mixf(a.z, b.z, t));
+}
+__device__ __forceinline__ float fractf(float x) { return x - floorf(x); }
+__device__ __forceinline__ float smoothstepf(float e0, float e1, float x) {
+  float t = clampf((x - e0) / (e1 - e0), 0.0f, 1.0f);
+  return t * t * (3.0f - 2.0f * t);
+}
+__device__ __forceinline__ float pow4(float x) {
+  float q = x * x;
+  return q * q;
+}
+
+struct Ctx {
+  const float *depth;
+  int dw, dh, dch;
+  int maxX, maxY;
+  float szw, szh;  // size.z, size.w
+  float tanh_, aspect;
+  float inv_near_minus_far, inv_far;
+};
+
+__device__ __forceinline__ float linear_depth(const Ctx &c, float d) {
+  float invZ = d * c.inv_near_minus_far + c.inv_far;
+  return 1.0f / fmaxf(invZ, 1e-6f);
+}
+__device__ __forceinline__ float fetch(const Ctx &c, int x, int y) {
+  x = min(max(x, 0), c.maxX);
+  y = min(max(y, 0), c.maxY);
+  return __ldg(c.depth + ((long)y * c.dw + x) * c.dch);
+}
+__device__ __forceinline__ v3 view_position(const Ctx &c, float u, float v, float z) {
+  float ndcX = u * 2.0f - 1.0f, ndcY = 1.0f - v * 2.0f;
+  return mk(ndcX * c.aspect * c.tanh_ * z, ndcY * c.tanh_ * z, -z);
+}
+__device__ __forceinline__ v3 view_position_at(const Ctx &c, int x, int y) {
+  float u = ((float)x + 0.5f) / c.szw, v = ((float)y + 0.5f) / c.szh;
+  return view_position(c, u, v, linear_depth(c, fetch(c, x, y)));
+}
+
+__device__ v3 reconstruct_normal(const Ctx &c, int x, int y) {
+  float cc = fetch(c, x, y);
+  float l1 = fetch(c, x - 1, y), l2 = fetch(c, x - 2, y);
+  float r1 = fetch(c, x + 1, y), r2 = fetch(c, x + 2, y);
+  float u1 = fetch(c, x, y - 1), u2 = fetch(c, x, y - 2);
+  float b1 = fetch(c, x, y + 1), b2 = fetch(c, x, y + 2);
+  float errL = fabsf(2.0f * l1 - l2 - cc), errR = fabsf(2.0f * r1 - r2 - cc);
+  float errU = fabsf(2.0f * u1 - u2 - cc), errB = fabsf(2.0f * b1 - b2 - cc);
+  // The five positions reuse the fetched disparities.
+  auto pos = [&](int px, int py, float d) {
+    float u = ((float)px + 0.5f) / c.szw, v = ((float)py + 0.5f) / c.szh;
+    return view_position(c, u, v, linear_depth(c, d));
+  };
+  // fetch() clamps coordinates; pos() must use the clamped coordinate's
+  // disparity but the unclamped pixel centre, as viewPositionAt does.
+  v3 pc = pos(x, y, cc);
+  v3 dxL = pc - pos(x - 1, y, l1);
+  v3 dxR = pos(x + 1, y, r1) - pc;
+  v3 dyU = pc - pos(x, y - 1, u1);
+  v3 dyD = pos(x, y + 1, b1) - pc;
+  v3 dx = errL < errR ? dxL : dxR;
+  v3 dy = errU < errB ? dyU : dyD;
+  v3 n = cross3(dy, dx);
+  float l = len3(n);
+  return l > 1e-12f ? divs(n, l) : mk(0, 0, 1);
+}
+
+__device__ float contact_shadow(const Ctx &c, v3 origin, v3 to_light, float max_len, float jitter, int steps) {
+  v3 step = (max_len / (float)steps) * to_light;
+  float occlusion = 0.0f;
+  v3 p = origin + jitter * step;
+  for (int i = 0; i < steps; i++) {
+    p = p + step;
+    float z = fmaxf(-p.z, 1e-4f);
+    float ndcX = p.x / (c.aspect * c.tanh_ * z);
+    float ndcY = p.y / (c.tanh_ * z);
+    float u = ndcX * 0.5f + 0.5f, v = 0.5f - ndcY * 0.5f;
+    if (u > 0.0f && u < 1.0f && v > 0.0f && v < 1.0f) {
+      int cx = (int)(u * c.szw), cy = (int)(v * c.szh);
+      float sceneZ = linear_depth(c, fetch(c, cx, cy));
+      float delta = -p.z - sceneZ;
+      float thickness = fmaxf(0.35f, sceneZ * 0.08f);
+      if (delta > 0.012f && delta < thickness) occlusion = fmaxf(occlusion, 1.0f - (float)i / (float)steps);
+    }
+  }
+  return 1.0f - clampf(occlusion, 0.0f, 1.0f);
+}
+
+__device__ float horizon_occlusion(const Ctx &c, int x, int y, v3 position, v3 normal, float radius_px,
+                                   float jitter, int dirs, int steps) {
+  float total = 0.0f;
+  for (int i = 0; i < dirs; i++) {
+    float angle = (((float)i + jitter) / (float)dirs) * 6.2831853f;
+    float s_, c_;
+    sincosf(angle, &s_, &c_);
+    float horizon = -1.0f;
+    for (int s = 0; s < steps; s++) {
+      float dist = radius_px * (((float)s + 1.0f) / (float)steps);
+      int sx = x + (int)(c_ * dist), sy = y + (int)(s_ * dist);
+      v3 diff = view_position_at(c, sx, sy) - position;
+      float l = len3(diff);
+      if (l > 1e-5f) {
+        float cosH = dot3(normal, divs(diff, l));
+        float falloff = clampf(1.0f - (l * l) / 9.0f, 0.0f, 1.0f);
+        horizon = fmaxf(horizon, cosH * falloff);
+      }
+    }
+    total += fmaxf(horizon, 0.0f);
+  }
+  return clampf(1.0f - total / (float)dirs, 0.0f, 1.0f);
+}
+
+__device__ __forceinline__ float ggx_d(float nDotH, float roughness) {
+  float r = fmaxf(roughness, 1e-3f);
+  float a = r * r;
+  float a2 = a * a;
+  float denom = nDotH * nDotH * (a2 - 1.0f) + 1.0f;
+  return a2 / (3.14159265f * denom * denom + 1e-20f);
+}
+__device__ __forceinline__ float smith_g(float nDotV, float nDotL, float roughness) {
+  float k = (roughness + 1.0f) * (roughness + 1.0f) / 8.0f;
+  return (nDotV / (nDotV * (1.0f - k) + k)) * (nDotL / (nDotL * (1.0f - k) + k));
+}
+__device__ __forceinline__ float srgb_to_linear(float v) {
+  return v <= 0.04045f ? v / 12.92f : powf((v + 0.055f) / 1.055f, 2.4f);
+}
+__device__ __forceinline__ float linear_to_srgb(float v) {
+  return v <= 0.0031308f ? 12.92f * v : 1.055f * powf(v, 1.0f / 2.4f) - 0.055f;
+}
+__device__ __forceinline__ float aces1(float x) {
+  return clampf((x * (2.51f * x + 0.03f)) / (x * (2.43f * x + 0.59f) + 0.14f), 0.0f, 1.0f);
+}
+__device__ __forceinline__ float reinhard1(float x) {
+  return clampf((x * (1.0f + x / 16.0f)) / (1.0f + x), 0.0f, 1.0f);
+}
+__device__ __forceinline__ uint32_t unorm8(float v) {
+  if (!(v > 0.0f)) return 0u;
+  if (v >= 1.0f) return 255u;
+  return (uint32_t)floorf(v * 255.0f + 0.5f);
+}
+
+struct LightSet {
+  ShadeLight l[8];
+};
+
+}  // namespace
+
+__global__ void __launch_bounds__(128) k_shade(const float *__restrict__ depth, int dw, int dh, int dch,
+                                               const float *__restrict__ albedo, int aw, int ah, LightSet L,
+                                               ShadeParams P, ShadeSteps st, int out_w, int out_h, float *hdr,
+                                               uint8_t *rgba8) {
+  int px = blockIdx.x * blockDim.x + threadIdx.x;
+  int py = blockIdx.y * blockDim.y + threadIdx.y;
+  if (px >= out_w || py >= out_h) return;
+  Ctx c;
+  c.depth = depth, c.dw = dw, c.dh = dh, c.dch = dch;
+  c.maxX = (int)P.size[2] - 1, c.maxY = (int)P.size[3] - 1;
+  c.szw = P.size[2], c.szh = P.size[3];
+  c.tanh_ = P.camera[0], c.aspect = P.camera[1];
+  float near = fmaxf(P.camera[2], 1e-3f), far = fmaxf(P.camera[3], near + 1e-3f);
+  c.inv_near_minus_far = 1.0f / near - 1.0f / far;
+  c.inv_far = 1.0f / far;
+
+  float u = ((float)px + 0.5f) / P.size[0], v = ((float)py + 0.5f) / P.size[1];
+  int dcx = (int)(u * P.size[2]), dcy = (int)(v * P.size[3]);
+  float disparity = fetch(c, dcx, dcy);
+  float z = linear_depth(c, disparity);
+  v3 position = view_position(c, u, v, z);
+  v3 rn = reconstruct_normal(c, dcx, dcy);
+  v3 normal = norm3(mk(rn.x * P.misc[3], rn.y * P.misc[3], rn.z));
+
+  // bilinear, clamp-to-edge albedo sample of the planar sRGB image
+  v3 alb_lin;
+  {
+    float tx = u * (float)aw - 0.5f, ty = v * (float)ah - 0.5f;
+    float fx0 = floorf(tx), fy0 = floorf(ty);
+    float fx = tx - fx0, fy = ty - fy0;
+    int x0 = min(max((int)fx0, 0), aw - 1), x1 = min(max((int)fx0 + 1, 0), aw - 1);
+    int y0 = min(max((int)fy0, 0), ah - 1), y1 = min(max((int)fy0 + 1, 0), ah - 1);
+    long plane = (long)aw * ah;
+    float ch[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+      const float *p = albedo + k * plane;
+      float a = __ldg(p + (long)y0 * aw + x0), b = __ldg(p + (long)y0 * aw + x1);
+      float cc = __ldg(p + (long)y1 * aw + x0), d = __ldg(p + (long)y1 * aw + x1);
+      float top = a + (b - a) * fx, bot = cc + (d - cc) * fx;
+      ch[k] = srgb_to_linear(top + (bot - top) * fy);
+    }
+    alb_lin = mk(ch[0], ch[1], ch[2]);
+  }
+  v3 albedo_c = mixv(mk(0.6f, 0.6f, 0.6f), alb_lin, P.debug[1]);
+  float fr = P.misc[0] * 5.588238f;
+  float jitter = fractf(52.9829189f * fractf((px + fr) * 0.06711056f + (py + fr) * 0.00583715f));
+  v3 view_dir = norm3(-1.0f * position);
+  float nDotV = fmaxf(dot3(normal, view_dir), 1e-4f);
+  float rough = clampf(P.misc[1], 0.04f, 1.0f);
+  float ao = 1.0f;
+  if (P.toggles[0] > 0.001f)
+    ao = mixf(1.0f, horizon_occlusion(c, dcx, dcy, position, normal, P.debug[3], jitter, st.ao_dirs, st.ao_steps),
+              P.toggles[0]);
+  v3 radiance = mulv((P.ambient[3] * ao) * albedo_c, mk(P.ambient[0], P.ambient[1], P.ambient[2]));
+  v3 scattering = mk(0, 0, 0);
+  float ray_len = len3(position);
+  v3 ray_dir = divs(position, fmaxf(ray_len, 1e-5f));
+
+  for (int li = 0; li < 8; li++) {
+    const ShadeLight &Lt = L.l[li];
+    float intensity = Lt.color[3];
+    if (!(intensity > 0.0f)) continue;
+    float kind = Lt.params[0];
+    v3 lcol = mk(Lt.color[0], Lt.color[1], Lt.color[2]);
+    v3 lpos = mk(Lt.position[0], Lt.position[1], Lt.position[2]);
+    v3 to_light = mk(0, 0, 1);
+    float atten = 1.0f, distance = 1e6f;
+    if (kind > 1.5f) {
+      to_light = norm3(-1.0f * lpos);
+    } else {
+      v3 delta = lpos - position;
+      distance = fmaxf(len3(delta), 1e-4f);
+      to_light = divs(delta, distance);
+      float range = fmaxf(Lt.params[2], 1e-3f);
+      float win = clampf(1.0f - pow4(distance / range), 0.0f, 1.0f);
+      atten = (win * win) / (distance * distance + 1e-4f);
+    }
+    v3 axis = mk(Lt.direction[0], Lt.direction[1], Lt.direction[2]);
+    if (kind > 0.5f && kind < 1.5f) {
+      float cosA = dot3(-1.0f * to_light, axis);
+      atten *= smoothstepf(Lt.direction[3], fmaxf(Lt.params[1], Lt.direction[3] + 1e-3f), cosA);
+    }
+    float nDotL = dot3(normal, to_light);
+    if (nDotL > 0.0f && atten > 0.0f) {
+      float shadow = 1.0f;
+      float amount = Lt.params[3] * P.toggles[1];
+      if (amount > 0.0f) {
+        float march = fminf(P.debug[2], distance);
+        shadow = mixf(1.0f, contact_shadow(c, position, to_light, march, jitter, st.contact), amount);
+      }
+      v3 half = norm3(to_light + view_dir);
+      float nDotH = fmaxf(dot3(normal, half), 0.0f);
+      float spec = ggx_d(nDotH, rough) * smith_g(nDotV, nDotL, rough) * P.fog[3];
+      float energy = atten * intensity * nDotL * shadow;
+      radiance = radiance + energy * mulv(lcol, albedo_c + mk(spec, spec, spec));
+    }
+    if (P.toggles[2] > 0.0f && kind < 1.5f) {
+      float step_len = ray_len / (float)st.volumetric;
+      float range = fmaxf(Lt.params[2], 1e-3f);
+      for (int s = 0; s < st.volumetric; s++) {
+        float t = (((float)s + jitter) / (float)st.volumetric) * ray_len;
+        v3 toL = lpos - t * ray_dir;
+        float dist = fmaxf(len3(toL), 1e-3f);
+        float win = clampf(1.0f - pow4(dist / range), 0.0f, 1.0f);
+        float att = (win * win) / (dist * dist + 1e-4f);
+        if (kind > 0.5f) {
+          float cosA = dot3(-1.0f * divs(toL, dist), axis);
+          att *= smoothstepf(Lt.direction[3], fmaxf(Lt.params[1], Lt.direction[3] + 1e-3f), cosA);
+        }
+        scattering = scattering + (att * intensity * step_len * P.misc[2]) * lcol;
+      }
+    }
+  }
+  radiance = radiance + P.toggles[2] * scattering;
+  float fog_amount = 1.0f - expf(-z * P.misc[2]);
+  radiance = mixv(radiance, mk(P.fog[0], P.fog[1], P.fog[2]), clampf(fog_amount, 0.0f, 1.0f));
+  radiance = P.toggles[3] * radiance;
+  float mode = P.debug[0];
+  v3 oc = radiance;
+  if (mode > 0.5f && mode < 1.5f) oc = mk(disparity, disparity, disparity);
+  else if (mode > 1.5f && mode < 2.5f) oc = 0.5f * (normal + mk(1, 1, 1));
+  else if (mode > 2.5f && mode < 3.5f) oc = mk(ao, ao, ao);
+  else if (mode > 3.5f) oc = alb_lin;
+
+  long o = (long)py * out_w + px;
+  if (hdr) reinterpret_cast<float4 *>(hdr)[o] = make_float4(oc.x, oc.y, oc.z, 1.0f);
+  if (rgba8) {
+    v3 mapped = P.grade[0] < 0.5f ? mk(aces1(oc.x), aces1(oc.y), aces1(oc.z))
+                                  : mk(reinhard1(oc.x), reinhard1(oc.y), reinhard1(oc.z));
+    float luma = dot3(mapped, mk(0.2126f, 0.7152f, 0.0722f));
+    v3 col = mixv(mk(luma, luma, luma), mapped, P.grade[2]);
+    col = mk(clampf(0.5f + P.grade[1] * (col.x - 0.5f), 0.0f, 1.0f),
+             clampf(0.5f + P.grade[1] * (col.y - 0.5f), 0.0f, 1.0f),
+             clampf(0.5f + P.grade[1] * (col.z - 0.5f), 0.0f, 1.0f));
+    float cu = u - 0.5f, cv = v - 0.5f;
+    float vig = 1.0f - P.grade[3] * (cu * cu + cv * cv) * 2.0f;
+    col = clampf(vig, 0.0f, 1.0f) * col;
+    uint32_t r = unorm8(linear_to_srgb(col.x)), g = unorm8(linear_to_srgb(col.y)), b = unorm8(linear_to_srgb(col.z));
+    reinterpret_cast<uint32_t *>(rgba8)[o] = r | (g << 8) | (b << 16) | (255u << 24);
+  }
+}
+
+cudaError_t shade(const float *depth, int dw, int dh, int dch, const float *albedo, int aw, int ah, const ShadeLight *lights,
+                  const ShadeParams &P, const ShadeSteps &steps, int out_w, int out_h, float *hdr, uint8_t *rgba8,
+                  cudaStream_t st) {
+  if (out_w <= 0 || out_h <= 0) return cudaSuccess;
+  LightSet L;
+  for (int i = 0; i < 8; i++) L.l[i] = lights[i];
+  dim3 block(16, 8);
+  dim3 grid((out_w + 15) / 16, (out_h + 7) / 8);
+  k_shade<<<grid, block, 0, st>>>(depth, dw, dh, dch, albedo, aw, ah, L, P, steps, out_w, out_h, hdr, rgba8);
+  return cudaGetLastError();
+}
+
+__global__ void k_resize(const float *src, int sw, int sh, float *dst, int dw, int dh) {
+  int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+  if (x >= dw || y >= dh) return;
+  float u = ((float)x + 0.5f) / (float)dw, v = ((float)y + 0.5f) / (float)dh;
+  float tx = u * (float)sw - 0.5f, ty = v * (float)sh - 0.5f;
+  float fx0 = floorf(tx), fy0 = floorf(ty);
+  float fx = tx - fx0, fy = ty - fy0;
+  int x0 = min(max((int)fx0, 0), sw - 1), x1 = min(max((int)fx0 + 1, 0), sw - 1);
+  int y0 = min(max((int)fy0, 0), sh - 1), y1 = min(max((int)fy0 + 1, 0), sh - 1);
+  float a = __ldg(src + (long)y0 * sw + x0), b = __ldg(src + (long)y0 * sw + x1);
+  float c = __ldg(src + (long)y1 * sw + x0), d = __ldg(src + (long)y1 * sw + x1);
+  float top = a + (b - a) * fx, bot = c + (d - c) * fx;
+  dst[(long)y * dw + x] = top + (bot - top) * fy;
+}
+
+cudaError_t resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh, cudaStream_t st) {
+  if (dw <= 0 || dh <= 0) return cudaSuccess;
+  dim3 block(32, 8), grid((dw + 31) / 32, (dh + 7) / 8);
+  k_resize<<<grid, block, 0, st>>>(src, sw, sh, dst, dw, dh);
+  return cudaGetLastError();
+}
+
+}  // namespace gpu
+}  // namespace illumina

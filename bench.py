@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""IlluminaDepth-448 on B200: batched frames/s (and batch-1 latency) vs roofline.
+
+Workload (one "step"): the whole hot path -- preprocess, 38 convolutions,
+head, joint-bilateral upsample -- over one batch of 256 synthetic 3x448x448
+fp32 frames (smooth blob images, seeded), with the seeded Kaiming weights
+(seed 0). Frames are independent, so N GPUs run N replicas on disjoint frame
+ranges with no collective on the data path (weak scaling); only the timing
+uses a barrier and a max-reduce.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0). The reference arm times the oracle port of the
+reference's CPU forward (src/model/reference.ts) on the host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "ai-illumination-depth-model_b200")
+for _p in (REPO, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "IlluminaDepth-448 batch-1 µs/frame and batched frames/s at 1/2/4/8 B200 vs roofline"
+UNIT = "frames/s"
+SIZE = 448
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--precision", default="f32", choices=["f32", "bf16"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip batch-1 latency and bf16 lines")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+# ---------------------------------------------------------------------------
+# measured peaks, clocks
+# ---------------------------------------------------------------------------
+
+def measured_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# algorithmic bytes / FLOPs per op (per frame), from the layer table
+# ---------------------------------------------------------------------------
+
+def op_algorithmic(arch, cost, elt=4):
+    """{op: (bytes, flops)} per frame: each distinct input and the output once, weights once per launch
+    (added by the caller), FLOPs = 2 x MACs (costOf)."""
+    t = arch.tensors
+    out = {}
+    for op, c in zip(arch.ops, cost.ops):
+        e = lambda n: t[n].h * t[n].w * t[n].c  # noqa: E731
+        if op.kind == "preprocess":
+            b = (SIZE * SIZE * 3 + e(op.out)) * 4
+        elif op.kind == "bilateralUp":
+            low = t[op.inp]
+            b = (low.h * low.w + SIZE * SIZE * 3 + SIZE * SIZE) * 4
+        elif op.kind == "head":
+            b = (e(op.inp) + t[op.out].h * t[op.out].w) * elt
+        elif op.kind == "lateral":
+            b = (e(op.coarse) + e(op.skip) + e(op.out)) * elt
+        else:
+            ins = [op.inp] + ([op.residual] if op.residual else [])
+            b = (sum(e(n) for n in ins) + e(op.out)) * elt
+        out[op.name] = (b, 2 * c.macs)
+    return out
+
+
+def weight_bytes_per_op(arch, specs):
+    import numpy as np
+    per = {}
+    for name, shape in specs:
+        op = name.rsplit(".", 1)[0]
+        per[op] = per.get(op, 0) + int(np.prod(shape)) * 4
+    return per
+
+
+def load_traffic():
+    try:
+        with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f)
+    except Exception:  # noqa: BLE001
+        return {}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle timing (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
+
+def cpu_oracle_frames_per_s(n_frames: int, threads: int):
+    """Times the oracle port of the reference CPU forward (preprocess -> 38 convs -> head ->
+    bilateralUp, double accumulation) on `n_frames` 448 blob-frame-shaped inputs across
+    `threads` host threads. Returns (frames/s, seconds)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import arch as OA
+    from oracle import lib as olib
+    from oracle import reference as R
+    from oracle import weights as OW
+    a = OA.build_architecture(SIZE)
+    w = OW.synthesize_weights(a, 0)
+    frames = []
+    for i in range(min(n_frames, threads)):
+        f = np.empty(3 * SIZE * SIZE, np.float32)
+        olib().or_uniform_frame(i, f.size, f.ctypes.data_as(C.POINTER(C.c_float)))
+        frames.append(f)
+
+    def one(i):
+        R.forward_frame(a, w, frames[i % len(frames)])
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(one, range(n_frames)))
+    dt = time.perf_counter() - t0
+    return n_frames / dt, dt
+
+
+def host_threads():
+    n = os.cpu_count() or 1
+    try:
+        n = len(os.sched_getaffinity(0))
+    except Exception:  # noqa: BLE001
+        pass
+    return max(1, min(n, 64))
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    threads = host_threads()
+    per_step = threads  # one 448 frame per thread per step (~1 s of CPU each)
+    for _ in range(max(0, args.warmup)):
+        cpu_oracle_frames_per_s(per_step, threads)
+    total_t, total_f = 0.0, 0
+    for _ in range(max(1, args.steps)):
+        _, dt = cpu_oracle_frames_per_s(per_step, threads)
+        total_t += dt
+        total_f += per_step
+    value = total_f / total_t
+    sample = f"{per_step} frames of 3x448x448 per step ({threads} threads, one frame each)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total_t / max(1, args.steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate/f32-store",
+        "data": "synthetic",
+        "config": {"workload": "illuminadepth448-forward-b256-blobs", "global_batch": args.batch * args.gpus,
+                   "input": "3x448x448 fp32", "weights": "synthesizeWeights(seed 0)",
+                   "note": "reference CPU path (src/model/reference.ts) as its oracle port; node is absent"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, local_rank, world):
+    import numpy as np
+    import torch
+
+    import illumina
+    from illumina import _lib
+
+    torch.cuda.set_device(local_rank)
+    pg = False
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+        pg = True
+
+    def barrier():
+        if pg:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if not pg:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B = args.batch
+    arch = illumina.buildArchitecture(SIZE)
+    cost = illumina.costOf(arch)
+    model = illumina.createDepthModel(arch, synthSeed=0, maxBatch=B, precision=args.precision, device=local_rank)
+    frames = torch.empty((B, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().illumina_generate_frames(1, rank * B, B, SIZE, frames.data_ptr(), None))
+    disp = torch.empty((B, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    launches = model.stats.launches
+
+    # ---- device-resident throughput (the value) ----
+    for _ in range(max(3, args.warmup)):
+        model.forward(frames, disparity=disp, stream=stream)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            model.forward(frames, disparity=disp, stream=stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms)
+    value = world * B * args.steps / (ms_max / 1000.0)
+    ms_per_step = ms_max / args.steps
+    stats = model.stats
+    launches = stats.launches
+
+    # ---- end to end through the C ABI with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        host_in = torch.empty((B, 3, SIZE, SIZE), dtype=torch.float32, pin_memory=True)
+        host_in.copy_(frames.cpu())
+        host_out = torch.empty((B, SIZE, SIZE), dtype=torch.float32, pin_memory=True)
+        hin, hout = host_in.numpy(), host_out.numpy()
+        for _ in range(2):
+            model.forward(hin, disparity=hout, stream=stream)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e_steps = max(3, min(args.steps, 10))
+        ev0.record(stream)
+        for _ in range(e_steps):
+            model.forward(hin, disparity=hout, stream=stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = max_over_ranks(ev0.elapsed_time(ev1))
+        e2e = {"value": world * B * e_steps / (e_ms / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
+               "steps": e_steps, "path": "illumina_forward (C ABI), pinned host buffers"}
+        del host_in, host_out
+
+    # ---- roofline of the dominant kernel (live CUDA events on the launching stream) ----
+    hbm, bf16, peak_src = measured_peaks()
+    roofline = None
+    per_op = {}
+    if rank == 0:
+        per_op = model.profile(frames, reps=2)
+        alg = op_algorithmic(arch, cost, elt=4 if args.precision == "f32" else 2)
+        wbytes = weight_bytes_per_op(arch, illumina.weightSpecs(arch))
+        top = max(per_op, key=per_op.get)
+        t_s = per_op[top] / 1000.0
+        bytes_launch = alg[top][0] * B + wbytes.get(top, 0)
+        flops_launch = alg[top][1] * B
+        achieved = bytes_launch / t_s / 1e9
+        traffic = load_traffic().get(f"{top}@b{B}-{args.precision}")
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "traffic": traffic, "kernel": top, "launch_ms": per_op[top],
+                    "algorithmic_bytes": bytes_launch, "flops": flops_launch,
+                    "fp32_tflops_achieved": flops_launch / t_s / 1e12,
+                    "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
+                    else "fallback 6.65 TB/s"}
+
+    # ---- extras: batch-1 latency (config 1) ----
+    extras = {}
+    if rank == 0 and not args.no_extras:
+        ring = 64  # 64 x 2.4 MB inputs > L2, so inputs are not cached between iterations
+        b1_frames = torch.empty((ring, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
+        _lib.check(_lib.lib().illumina_generate_frames(0, 0, ring, SIZE, b1_frames.data_ptr(), None))
+        b1_out = torch.empty((1, SIZE, SIZE), dtype=torch.float32, device="cuda")
+        views = [b1_frames[i:i + 1] for i in range(ring)]
+        for v in views:
+            model.forward(v, disparity=b1_out, stream=stream)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        reps = 200
+        for i in range(reps):
+            model.forward(views[i % ring], disparity=b1_out, stream=stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        extras["batch1_us_per_frame"] = 1000.0 * ev0.elapsed_time(ev1) / reps
+        del b1_frames
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        n = threads * 2
+        fps, dt = cpu_oracle_frames_per_s(n, threads)
+        cpu = {"value": fps, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{n} frames of 3x448x448 ({dt:.1f} s over {threads} threads); oracle port of "
+                         "src/model/reference.ts (double accumulation, f32 storage) + bilateralUp"}
+
+    model.destroy()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+            "config": {"workload": f"illuminadepth448-forward-b{B}-blobs", "model": "IlluminaDepth-448",
+                       "global_batch": B * world, "per_gpu_batch": B, "input": "3x448x448 fp32 blob frames",
+                       "weights": "synthesizeWeights(seed 0)", "parallelism": f"replicas x{world} (frames sharded)",
+                       "l2": f"inputs {B * 3 * SIZE * SIZE * 4 / 1e6:.0f} MB per step > 126 MB L2",
+                       "precision": args.precision},
+            "e2e": e2e, "gpu_launches": launches * args.steps, "launches_per_step": launches,
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), **extras,
+            "per_op_ms": {k: round(v, 4) for k, v in per_op.items()} if per_op else None,
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    rank, local_rank, world = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, local_rank, world)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

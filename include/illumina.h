@@ -1,0 +1,322 @@
+/*
+ * illumina.h -- C ABI of the B200-native IlluminaDepth hot path.
+ *
+ * One shared library (libillumina.so) replaces the reference's WebGPU runner,
+ * kernels and lighting pass. Every entry point is plain C: pointers, sizes and
+ * status codes, no C++ or torch types. A node-api addon (or any FFI) binds
+ * them 1:1 and turns a non-OK status into `throw new Error(illumina_last_error())`.
+ *
+ * Pointers: frame, disparity and tensor arguments may be host memory (pageable
+ * or pinned) or device memory of the model's device, unless an entry point says
+ * "device". `stream` is a cudaStream_t (NULL = the legacy default stream).
+ *
+ * Threading: one model per device; calls on one model are not re-entrant. Use
+ * one host thread per device for multi-GPU work. illumina_last_error() is
+ * thread-local.
+ *
+ * Each declaration names the reference interface it replaces (file:line within
+ * the reference project).
+ */
+#ifndef ILLUMINA_H
+#define ILLUMINA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The message for the last failure on this thread is in
+ * illumina_last_error(); weight errors use the reference's wording
+ * (src/model/weights.ts:97-165). */
+typedef enum illumina_status {
+  ILLUMINA_OK = 0,
+  ILLUMINA_INVALID_ARG = 1,
+  ILLUMINA_BAD_WEIGHTS = 2,
+  ILLUMINA_ARCH_MISMATCH = 3,
+  ILLUMINA_CUDA_ERROR = 4,
+  ILLUMINA_TIMEOUT = 5,
+  ILLUMINA_NO_DEVICE = 6
+} illumina_status;
+
+/* Activation ids (src/model/arch.ts:32, src/model/layout.ts:131-142). */
+enum { ILLUMINA_ACT_LINEAR = 0, ILLUMINA_ACT_RELU = 1, ILLUMINA_ACT_RELU6 = 2, ILLUMINA_ACT_HARDSWISH = 3 };
+
+/* Arithmetic of the network: fp32 everywhere, or bf16 storage of activations
+ * and weights with fp32 accumulation. */
+enum { ILLUMINA_PRECISION_F32 = 0, ILLUMINA_PRECISION_BF16 = 1 };
+
+/* Frame layouts accepted by the forward pass. Components in [0, 1]. */
+enum {
+  ILLUMINA_FRAME_RGB_PLANAR = 0,     /* N x 3 x S x S float32  */
+  ILLUMINA_FRAME_RGBA_INTERLEAVED = 1 /* N x S x S x 4 float32, alpha ignored */
+};
+
+/* Last error message of this thread ("" when none). */
+const char *illumina_last_error(void);
+/* Library version string. */
+const char *illumina_version(void);
+/* Number of CUDA devices visible to the library (0 without a GPU). */
+int illumina_device_count(void);
+
+/* ---------------------------------------------------------------------------
+ * Layer table, weights, arena (pure host logic; no GPU needed)
+ * ------------------------------------------------------------------------- */
+
+/* buildArchitecture + costOf + weightSpecs (src/model/arch.ts:191-489,
+ * src/model/weights.ts:29-63) as one JSON document:
+ * {"name","inputSize","mean","std","tensors":{name:[h,w,c]},"ops":[...],
+ *  "cost":[{"name","kind","macs","params"}],"totalMacs","totalParams",
+ *  "specs":[[name,[shape]]]}. Writes at most `cap` bytes (NUL-terminated) and
+ * stores the required size (including the NUL) in *needed. */
+illumina_status illumina_arch_json(int input_size, char *buf, size_t cap, size_t *needed);
+
+/* planArena + validateArena (src/engine/arena.ts:57-172) with the runner's
+ * exclusion of the `depth` tensor (src/model/runner.ts:190-192), as JSON:
+ * {"bufferSizes":[vec4 counts],"assignment":{name:index},"totalBytes","naiveBytes"}. */
+illumina_status illumina_arena_json(int input_size, char *buf, size_t cap, size_t *needed);
+
+/* Total float count of the weight blob (all tensors of weightSpecs, in order). */
+illumina_status illumina_weights_count(int input_size, size_t *count);
+
+/* synthesizeWeights(arch, seed) (src/model/weights.ts:227-251) into a flat
+ * float blob in weightSpecs order. */
+illumina_status illumina_weights_synthesize(int input_size, uint32_t seed, float *out, size_t count);
+
+/* parseWeights (src/model/weights.ts:97-165): validates an idm/1 container
+ * (f32 or f16 tensors) and writes the flat blob in weightSpecs order.
+ * Errors: ILLUMINA_BAD_WEIGHTS or ILLUMINA_ARCH_MISMATCH with the reference's
+ * messages. */
+illumina_status illumina_weights_parse(int input_size, const void *bytes, size_t len, float *out,
+                                       size_t count);
+
+/* serializeWeights (src/model/weights.ts:168-194): flat blob -> idm/1 bytes
+ * (compact JSON header, f32 tensors). *needed receives the byte size. */
+illumina_status illumina_weights_serialize(int input_size, const float *blob, size_t count, void *out,
+                                           size_t cap, size_t *needed);
+
+/* halfToFloat (src/model/weights.ts:82-95). */
+double illumina_half_to_float(uint16_t h);
+
+/* ---------------------------------------------------------------------------
+ * Depth model (createDepthModel / DepthModel, src/model/runner.ts:79-485)
+ * ------------------------------------------------------------------------- */
+
+typedef struct illumina_model illumina_model;
+
+typedef struct illumina_model_options {
+  int input_size;          /* network resolution, multiple of 32 (arch.ts:191) */
+  int device;              /* CUDA device ordinal */
+  int max_batch;           /* largest frame count per forward call */
+  int precision;           /* ILLUMINA_PRECISION_* */
+  int decode_srgb;         /* DepthModelOptions.decodeSrgb (runner.ts:90-91) */
+  float exposure;          /* DepthModelOptions.exposure (runner.ts:92) */
+  float range_sigma;       /* DepthPostParams x (runner.ts:185-187), 0.12 */
+  float temporal_base;     /* DepthPostParams y, 0.35 */
+  float temporal_sensitivity; /* DepthPostParams z, 3.0 */
+  int keep_intermediates;  /* 1: no arena aliasing, every tensor stays readable */
+  /* Weights, first non-empty source wins: flat blob, .idm bytes, .idm path,
+   * else synthesizeWeights(arch, synth_seed) (the app's fallback, main.ts:61). */
+  const float *weights;
+  size_t weights_count;
+  const void *idm_bytes;
+  size_t idm_len;
+  const char *idm_path;
+  uint32_t synth_seed;
+} illumina_model_options;
+
+/* Defaults: 448, device 0, batch 1, fp32, sRGB on, exposure 1, (0.12, 0.35,
+ * 3.0), aliased arena, synthetic seed 1. */
+void illumina_model_options_default(illumina_model_options *opts);
+
+/* createDepthModel (runner.ts:160-485): parses/validates weights, plans and
+ * validates the arena, uploads and packs weights once, allocates one device
+ * arena sized for max_batch. Nothing is allocated per forward afterwards. */
+illumina_status illumina_model_create(const illumina_model_options *opts, illumina_model **out);
+/* DepthModel.destroy (runner.ts:478-484). */
+illumina_status illumina_model_destroy(illumina_model *model);
+/* DepthModel.setExposure (runner.ts:456-460). */
+illumina_status illumina_model_set_exposure(illumina_model *model, float exposure);
+/* DepthModel.setTemporal (runner.ts:461-465). */
+illumina_status illumina_model_set_temporal(illumina_model *model, float base_alpha,
+                                            float motion_sensitivity, float range_sigma);
+
+/* The whole hot path for n independent frames (first-frame temporal
+ * semantics, io.ts:259-266): preprocess -> 38 convolutions -> head ->
+ * bilateralUp. `disparity` receives n x S x S float32 (the `depth` texture's
+ * x channel); `depth_low` (nullable) receives n x S/2 x S/2 float32 (head
+ * output, channel 0). The launch sequence is captured once per distinct
+ * (n, pointers) and replayed as a CUDA graph. */
+illumina_status illumina_forward(illumina_model *model, const float *frames, int n, int frame_layout,
+                                 float *disparity, float *depth_low, void *stream);
+
+/* DepthModel.record for one streaming frame (runner.ts:440-449): like
+ * illumina_forward with n = 1, but the bilateral upsample blends with the
+ * temporal history held in the model's depth ping-pong and writes the depth
+ * texture (stabilised, raw, change, 1) into slot outputParity(). */
+illumina_status illumina_model_record(illumina_model *model, const float *frame, int frame_layout,
+                                      void *stream);
+/* DepthModel.swapHistory / outputParity / freshParity (runner.ts:450-454). */
+illumina_status illumina_model_swap_history(illumina_model *model);
+int illumina_model_output_parity(const illumina_model *model);
+int illumina_model_fresh_parity(const illumina_model *model);
+/* DepthModel.debugDepth (runner.ts:455): device pointer of depth slot `index`
+ * (S x S x 4 float32: stabilised, raw, change, validity). */
+illumina_status illumina_model_depth_slot(illumina_model *model, int index, const float **device_ptr);
+
+/* DepthModel.debugTensor (runner.ts:466-476): copies frame 0 of tensor `name`
+ * (h x w x c float32, channels-last) into `out` (host or device, at most
+ * `cap` floats) and reports whether the tensor still owns its arena buffer
+ * after a full forward (live_at_end = 0 when a later tensor reused it). */
+illumina_status illumina_model_debug_tensor(illumina_model *model, const char *name, float *out,
+                                            size_t cap, int *h, int *w, int *c, int *live_at_end);
+
+/* DepthModel.stats (runner.ts:95-101, :425-434). */
+typedef struct illumina_stats {
+  int dispatches;          /* ops in the layer table (40) */
+  int launches;            /* kernels one forward launches */
+  size_t arena_bytes;      /* aliased activation bytes per frame (fp32 accounting) */
+  size_t naive_arena_bytes;/* one buffer per tensor, per frame */
+  size_t weight_bytes;     /* logical weight bytes (fp32) */
+  size_t device_bytes;     /* device memory the model holds */
+  int max_batch;
+  int precision;
+  int input_size;
+} illumina_stats;
+illumina_status illumina_model_stats(const illumina_model *model, illumina_stats *out);
+
+/* GpuProfiler analogue (src/engine/timing.ts:48-191): runs the op list
+ * `reps` times as individual launches on the model's stream with a CUDA event
+ * between consecutive ops, and writes the mean device time of each op in
+ * milliseconds to op_ms[0..40) (an op fused into its neighbour reports 0).
+ * `frames` must be device memory. For profiling only; the forward path
+ * replays the captured graph instead. */
+illumina_status illumina_model_profile(illumina_model *model, const float *frames, int n, int frame_layout,
+                                       int reps, float *op_ms, int cap);
+
+/* ---------------------------------------------------------------------------
+ * Per-kernel entry points (the kernel factories under src/model/kernels/).
+ * All pointers are device pointers; weights are in the logical .idm layout.
+ * ------------------------------------------------------------------------- */
+
+/* makePointwise (kernels/pointwise.ts:64-133): dst[p][oc] = act(b[oc] +
+ * sum_ic w[oc][ic]*src[p][ic] (+ res[p][oc])). */
+illumina_status illumina_op_pointwise(const float *src, long pixels, int in_c, const float *w,
+                                      const float *b, int out_c, int act, const float *res, float *dst,
+                                      void *stream);
+
+/* makeDepthwisePointwise (kernels/dwpw.ts:165-296): depthwise k x k stride s
+ * (+dw_b, mid_act) then 1x1 (+pw_b, +res, act). dw_w is [in_c][k][k]. */
+illumina_status illumina_op_dwpw(const float *src, int in_h, int in_w, int in_c, const float *dw_w,
+                                 const float *dw_b, int mid_act, const float *pw_w, const float *pw_b,
+                                 int out_c, int k, int stride, int act, const float *res, float *dst,
+                                 void *stream);
+
+/* makeConv (kernels/conv.ts:94-168): dense k x k stride s, zero pad, w is
+ * [out_c][in_c][k][k]. */
+illumina_status illumina_op_conv(const float *src, int in_h, int in_w, int in_c, const float *w,
+                                 const float *b, int out_c, int k, int stride, int act, float *dst,
+                                 void *stream);
+
+/* makeLateral (kernels/lateral.ts:46-169): act(b + up2(coarse) + W skip);
+ * coarse is ch x cw x out_c, skip is 2ch x 2cw x skip_c, w is [out_c][skip_c]. */
+illumina_status illumina_op_lateral(const float *coarse, int ch, int cw, const float *skip, int skip_c,
+                                    const float *w, const float *b, int out_c, int act, float *dst,
+                                    void *stream);
+
+/* makeHead (kernels/io.ts:141-166): dst4[p] = sigmoid(b + w.src[p]) x 4. */
+illumina_status illumina_op_head(const float *src, long pixels, int in_c, const float *w, float b,
+                                 float *dst4, void *stream);
+
+/* makePreprocess (kernels/io.ts:64-118) for a source already at network
+ * resolution: frames (layout as above) -> input tensor (S x S x 4) and
+ * sceneColor (S x S x 4, nullable). */
+illumina_status illumina_op_preprocess(const float *frames, int n, int frame_layout, int size,
+                                       int decode_srgb, float exposure, float *input, float *scene_color,
+                                       void *stream);
+
+/* makeDepthUpsample (kernels/io.ts:203-283), first frame: low is lh x lw x
+ * low_c (channel 0 read), guide is (2lh) x (2lw) x guide_c linear colour,
+ * dst is (2lh) x (2lw) float32. */
+illumina_status illumina_op_bilateral(const float *low, int lh, int lw, int low_c, const float *guide,
+                                      int guide_c, float range_sigma, float *dst, void *stream);
+
+/* ---------------------------------------------------------------------------
+ * Lighting (src/lighting/)
+ * ------------------------------------------------------------------------- */
+
+#define ILLUMINA_MAX_LIGHTS 8 /* lights.ts:147 */
+
+/* Light struct, field for field (lights.ts:132-144). */
+typedef struct illumina_light {
+  float position[4];  /* xyz view-space position (direction for directional) */
+  float color[4];     /* rgb linear colour, a = intensity (0 = slot unused) */
+  float direction[4]; /* xyz spot axis, w = cos(outer cone) */
+  float params[4];    /* x kind (0 point, 1 spot, 2 directional), y cos(inner), z radius, w shadow */
+} illumina_light;
+
+/* ShadingSettings, field for field (renderer.ts:53-78). */
+typedef struct illumina_shading_settings {
+  float fov_y, near_m, far_m;
+  float ao_strength, shadow_strength, volumetric, exposure;
+  float ambient[3];
+  float ambient_intensity, roughness, fog_density;
+  float fog_color[3];
+  float specular, normal_strength, albedo_mix, contact_shadow_length, ao_radius_pixels;
+  int tone_map; /* 0 ACES fitted, 1 Reinhard */
+  float contrast, saturation, vignette;
+  int debug_view; /* 0 lit, 1 depth, 2 normals, 3 occlusion, 4 albedo */
+} illumina_shading_settings;
+
+/* DEFAULT_SETTINGS (renderer.ts:80-103). */
+void illumina_shading_settings_default(illumina_shading_settings *s);
+
+/* March step counts. The reference compiles contact 12 (shade.ts:192), AO
+ * 6 directions x 4 steps (:232-233) and 10 volumetric steps per light (:310). */
+typedef struct illumina_shade_steps {
+  int contact, ao_dirs, ao_steps, volumetric;
+} illumina_shade_steps;
+
+/* makeShade + composite (shade.ts:312-528, composite.ts:87-113) in one pass:
+ * disparity is dh x dw texels of `disparity_channels` float32 each (channel 0
+ * read, nearest fetch; 4 reads a depth slot directly), albedo is a 3 x ah x aw
+ * sRGB image (bilinear, clamp-to-edge), lights is ILLUMINA_MAX_LIGHTS slots.
+ * `steps` NULL selects the reference's constants. Outputs (either nullable):
+ * hdr (out_h x out_w x 4 float32, the HDR target) and rgba8 (out_h x out_w x 4
+ * bytes, tone-mapped 8-bit sRGB). Device pointers only. */
+illumina_status illumina_shade(const float *disparity, int dw, int dh, int disparity_channels,
+                               const float *albedo, int aw,
+                               int ah, const illumina_light *lights,
+                               const illumina_shading_settings *settings, uint32_t frame,
+                               const illumina_shade_steps *steps, int out_w, int out_h, float *hdr,
+                               uint8_t *rgba8, void *stream);
+
+/* Bilinear resize of a single-channel map (align_corners=false, edge clamp),
+ * used to bring the disparity to render resolution. Device pointers. */
+illumina_status illumina_resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh,
+                                         void *stream);
+
+/* ---------------------------------------------------------------------------
+ * Synthetic workloads and checksums
+ * ------------------------------------------------------------------------- */
+
+enum { ILLUMINA_FRAMES_UNIFORM = 0, ILLUMINA_FRAMES_BLOBS = 1 };
+
+/* Seeded frames on the device, 3 x size x size planar each; frame i uses seed
+ * seed0 + i. UNIFORM: float32 of mulberry32 draws in (c, y, x) order. BLOBS:
+ * 8 anisotropic Gaussian blobs per channel + N(0, 0.02) noise, clamped. */
+illumina_status illumina_generate_frames(int kind, uint32_t seed0, int n, int size, float *out,
+                                         void *stream);
+
+/* Per-frame checksums of n maps of `count` float32 each (device pointer):
+ * sum64[i] = sum_j bits(x_j) * (2j + 1) mod 2^64 and fsum[i] = sum_j x_j
+ * (double). Outputs are device pointers. */
+illumina_status illumina_checksums(const float *maps, int n, long count, uint64_t *sum64, double *fsum,
+                                   void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ILLUMINA_H */
