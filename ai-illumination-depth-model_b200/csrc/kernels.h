@@ -17,6 +17,12 @@ struct PreprocessParams {
   int decode_srgb;
 };
 
+// Argument positions of the kernels whose pointer arguments a replayed CUDA
+// graph re-targets (cudaGraphExecKernelNodeSetParams); they must match the
+// parameter lists of k_preprocess and k_bilateral in net_kernels.cu.
+constexpr int kPreprocessArgCount = 8, kPreprocessFramesArg = 0;
+constexpr int kBilateralArgCount = 12, kBilateralDstArg = 9;
+
 // frames (layout 0 planar / 1 rgba) -> input (n*S*S*4, storage T), luma (n*S*S
 // f32), scene (n*S*S*4 f32, nullable).
 cudaError_t preprocess(int T, const float *frames, int layout, int n, int S, const PreprocessParams &p,
@@ -27,12 +33,12 @@ cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const flo
                  int Cout, int k, int stride, int act, void *dst, cudaStream_t st);
 
 struct GemmOp {
-  int mode;  // 0 pointwise, 1 depthwise->pointwise, 2 lateral
-  const void *src;   // pw: [M][K]; dw: (n,H,W,K); lateral: skip [M][K]
-  const float *w;    // [N][K] f32
-  const float *bias; // [N]
-  const void *res;   // [M][N] or null
-  void *dst;         // [M][N]
+  int mode = 0;                  // 0 pointwise, 1 depthwise->pointwise, 2 lateral
+  const void *src = nullptr;     // pw: [M][K]; dw: (n,H,W,K); lateral: skip [M][K]
+  const float *w = nullptr;      // [N][K] f32
+  const float *bias = nullptr;   // [N]
+  const void *res = nullptr;     // [M][N] or null
+  void *dst = nullptr;           // [M][N]
   int n = 1;         // frames
   int H = 0, W = 0;  // dw: input spatial; lateral: output spatial
   int OH = 0, OW = 0;// output spatial (dw) ; pw: OH*OW*n = M

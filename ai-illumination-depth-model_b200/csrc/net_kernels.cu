@@ -87,6 +87,7 @@ static inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + 
 // preprocess (src/model/kernels/io.ts:64-118 semantics, refPreprocess)
 // ---------------------------------------------------------------------------
 
+// Parameter list mirrored by kPreprocessArgCount / kPreprocessFramesArg.
 template <typename T>
 __global__ void k_preprocess(const float *__restrict__ frames, int layout, long total, int S, PreprocessParams p,
                              T *__restrict__ input, float *__restrict__ luma, float *__restrict__ scene) {
@@ -474,6 +475,7 @@ cudaError_t head(int T, const void *src, long M, int C, const float *w, float bi
 
 // low: (n, lh, lw) with channel stride lc; guide luma either precomputed
 // (luma, 1 channel) or from linear colour (guide, gc channels).
+// Parameter list mirrored by kBilateralArgCount / kBilateralDstArg.
 __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh, int lw,
                             const float *__restrict__ luma, const float *__restrict__ guide, int gc,
                             BilateralParams p, float *__restrict__ dst, const float *__restrict__ history,

@@ -67,13 +67,28 @@ bool is_device_ptr(const void *p) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// A captured forward is keyed by its shape; the caller's frame / disparity /
+// depth_low pointers are re-targeted in place on replay.
 struct GraphKey {
-  int n, layout, mode;
-  const void *frames, *disp, *low, *hist, *tex;
+  int n, layout, mode, has_low;
+  const void *hist, *tex;
   bool operator==(const GraphKey &o) const {
-    return n == o.n && layout == o.layout && mode == o.mode && frames == o.frames && disp == o.disp &&
-           low == o.low && hist == o.hist && tex == o.tex;
+    return n == o.n && layout == o.layout && mode == o.mode && has_low == o.has_low && hist == o.hist &&
+           tex == o.tex;
   }
+};
+
+// Graph nodes whose pointer arguments depend on the caller's buffers.
+struct CaptureNodes {
+  cudaGraphNode_t pre = nullptr, bil = nullptr, low = nullptr;
+};
+
+struct GraphEntry {
+  GraphKey key;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  CaptureNodes nodes;
+  const void *frames = nullptr, *disp = nullptr, *low = nullptr;
 };
 
 struct OpWeights {
@@ -106,7 +121,7 @@ struct illumina_model {
   size_t device_bytes = 0;
   int history_index = 0, last_written = 1;
   float exposure = 1, range_sigma = 0.12f, base_alpha = 0.35f, sensitivity = 3.0f;
-  std::vector<std::pair<GraphKey, cudaGraphExec_t>> graphs;
+  std::vector<GraphEntry> graphs;
   int launches_per_forward = 0;
 
   void *tensor(const std::string &name) {
@@ -115,7 +130,10 @@ struct illumina_model {
     return d_arena + buf_off[it->second];
   }
   void clear_graphs() {
-    for (auto &g : graphs) cudaGraphExecDestroy(g.second);
+    for (auto &g : graphs) {
+      cudaGraphExecDestroy(g.exec);
+      cudaGraphDestroy(g.graph);
+    }
     graphs.clear();
   }
   ~illumina_model();
@@ -166,8 +184,20 @@ gpu::PreprocessParams preprocess_params(const illumina_model &m) {
 
 // Enqueues the whole op list on m.stream. mode 0: independent frames -> disp;
 // mode 1: streaming frame with history (n == 1).
+// The node most recently added to the graph being captured on `st`.
+cudaGraphNode_t last_captured_node(cudaStream_t st) {
+  cudaStreamCaptureStatus status;
+  const cudaGraphNode_t *deps = nullptr;
+  size_t nd = 0;
+  cuda_check(cudaStreamGetCaptureInfo(st, &status, nullptr, nullptr, &deps, &nd), "capture info");
+  if (status != cudaStreamCaptureStatusActive || nd != 1 || !deps)
+    throw Error(ILLUMINA_CUDA_ERROR, "graph capture: expected a single tail node");
+  return deps[0];
+}
+
 int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, float *disp, float *low_out,
-                    const float *history, float *out_tex, const std::vector<cudaEvent_t> *marks = nullptr) {
+                    const float *history, float *out_tex, const std::vector<cudaEvent_t> *marks = nullptr,
+                    CaptureNodes *nodes = nullptr) {
   const Architecture &a = m.arch;
   const int S = a.input_size;
   int launches = 0;
@@ -181,6 +211,7 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
         cuda_check(gpu::preprocess(m.T, frames, layout, n, S, preprocess_params(m), m.tensor(op.out), m.d_luma,
                                    m.d_scene, st),
                    "preprocess");
+        if (nodes) nodes->pre = last_captured_node(st);
         launches++;
         break;
       case OpKind::Conv: {
@@ -237,6 +268,7 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
         launches++;
         if (low_out) {
           cuda_check(cudaMemcpyAsync(low_out, low, sizeof(float) * M, cudaMemcpyDeviceToDevice, st), "depth_low copy");
+          if (nodes) nodes->low = last_captured_node(st);
         }
         break;
       }
@@ -246,6 +278,7 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
         cuda_check(gpu::bilateral((const float *)m.tensor(op.in), n, si.h, si.w, m.d_luma, bp, disp, history,
                                   out_tex, st),
                    "bilateralUp");
+        if (nodes) nodes->bil = last_captured_node(st);
         launches++;
         break;
       }
@@ -255,33 +288,66 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
   return launches;
 }
 
-cudaGraphExec_t graph_for(illumina_model &m, const GraphKey &key, const float *frames, float *disp, float *low,
-                          const float *hist, float *tex) {
-  for (auto &g : m.graphs)
-    if (g.first == key) return g.second;
+// Re-targets pointer argument `arg` of kernel node `node` in `e.exec`.
+void patch_kernel_arg(GraphEntry &e, cudaGraphNode_t node, int nargs, int arg, const void *value) {
+  cudaKernelNodeParams kp;
+  cuda_check(cudaGraphKernelNodeGetParams(node, &kp), "kernel node params");
+  std::vector<void *> args(kp.kernelParams, kp.kernelParams + nargs);
+  const void *v = value;
+  args[arg] = &v;
+  kp.kernelParams = args.data();
+  cuda_check(cudaGraphExecKernelNodeSetParams(e.exec, node, &kp), "retarget kernel node");
+}
+
+GraphEntry &graph_for(illumina_model &m, const GraphKey &key, const float *frames, float *disp, float *low,
+                      const float *hist, float *tex) {
+  for (auto &g : m.graphs) {
+    if (!(g.key == key)) continue;
+    if (g.frames != frames) {
+      patch_kernel_arg(g, g.nodes.pre, gpu::kPreprocessArgCount, gpu::kPreprocessFramesArg, frames);
+      g.frames = frames;
+    }
+    if (g.disp != disp) {
+      patch_kernel_arg(g, g.nodes.bil, gpu::kBilateralArgCount, gpu::kBilateralDstArg, disp);
+      g.disp = disp;
+    }
+    if (low && g.low != low) {
+      const TensorShape &ls = m.arch.shape("depth_low");
+      size_t bytes = sizeof(float) * (size_t)key.n * ls.h * ls.w;
+      cuda_check(cudaGraphExecMemcpyNodeSetParams1D(g.exec, g.nodes.low, low, m.tensor("depth_low"), bytes,
+                                                    cudaMemcpyDeviceToDevice),
+                 "retarget memcpy node");
+      g.low = low;
+    }
+    return g;
+  }
   if (m.graphs.size() >= 8) {
-    cudaGraphExecDestroy(m.graphs.front().second);
+    cudaGraphExecDestroy(m.graphs.front().exec);
+    cudaGraphDestroy(m.graphs.front().graph);
     m.graphs.erase(m.graphs.begin());
   }
+  GraphEntry e;
+  e.key = key;
   cuda_check(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal), "begin capture");
   int launches = 0;
   try {
-    launches = enqueue_forward(m, key.n, frames, key.layout, disp, low, hist, tex);
+    launches = enqueue_forward(m, key.n, frames, key.layout, disp, low, hist, tex, nullptr, &e.nodes);
   } catch (...) {
     cudaGraph_t g = nullptr;
     cudaStreamEndCapture(m.stream, &g);
     if (g) cudaGraphDestroy(g);
     throw;
   }
-  cudaGraph_t graph = nullptr;
-  cuda_check(cudaStreamEndCapture(m.stream, &graph), "end capture");
-  cudaGraphExec_t exec = nullptr;
-  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
-  cudaGraphDestroy(graph);
-  cuda_check(e, "graph instantiate");
+  cuda_check(cudaStreamEndCapture(m.stream, &e.graph), "end capture");
+  cudaError_t err = cudaGraphInstantiate(&e.exec, e.graph, 0);
+  if (err != cudaSuccess) {
+    cudaGraphDestroy(e.graph);
+    cuda_check(err, "graph instantiate");
+  }
+  e.frames = frames, e.disp = disp, e.low = low;
   m.launches_per_forward = launches;
-  m.graphs.push_back({key, exec});
-  return exec;
+  m.graphs.push_back(e);
+  return m.graphs.back();
 }
 
 // Runs the hot path with caller pointers (host or device). Host pointers are
@@ -323,9 +389,9 @@ void run_forward(illumina_model &m, const float *frames, int n, int layout, floa
     hist = m.d_tex[m.history_index];
     tex = m.d_tex[1 - m.history_index];
   }
-  GraphKey key{n, layout, mode, f_dev, d_disp, d_low, hist, tex};
-  cudaGraphExec_t exec = graph_for(m, key, f_dev, d_disp, d_low, hist, tex);
-  cuda_check(cudaGraphLaunch(exec, m.stream), "graph launch");
+  GraphKey key{n, layout, mode, d_low ? 1 : 0, hist, tex};
+  GraphEntry &g = graph_for(m, key, f_dev, d_disp, d_low, hist, tex);
+  cuda_check(cudaGraphLaunch(g.exec, m.stream), "graph launch");
 
   if (host_disp)
     cuda_check(cudaMemcpyAsync(disp, m.d_stage_out, sizeof(float) * n * disp_floats, cudaMemcpyDeviceToHost, m.stream),

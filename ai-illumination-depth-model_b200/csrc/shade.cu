@@ -160,7 +160,7 @@ __device__ __forceinline__ float ggx_d(float nDotH, float roughness) {
   float r = fmaxf(roughness, 1e-3f);
   float a = r * r;
   float a2 = a * a;
-  float denom = nDotH * nDotH * (a2 - 1.0f) + 1.0f;
+  float denom = fmaf(nDotH * nDotH, a2 - 1.0f, 1.0f);  // one rounding, as the oracle
   return a2 / (3.14159265f * denom * denom + 1e-20f);
 }
 __device__ __forceinline__ float smith_g(float nDotV, float nDotL, float roughness) {

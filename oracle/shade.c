@@ -188,7 +188,9 @@ float or_ggx_d(float nDotH, float roughness) {
   float r = fmaxw(roughness, 1e-3f);
   float a = r * r;
   float a2 = a * a;
-  float denom = nDotH * nDotH * (a2 - 1.0f) + 1.0f;
+  /* One fused multiply-add, as the CUDA kernel (and GPU shader compilers)
+   * evaluate it, so both sides round identically. */
+  float denom = fmaf(nDotH * nDotH, a2 - 1.0f, 1.0f);
   return a2 / (3.14159265f * denom * denom + 1e-20f);
 }
 

@@ -148,6 +148,26 @@ def test_batched_forward_equals_per_frame(torch):
     m.destroy()
 
 
+def test_graph_replay_retargets_caller_buffers(torch):
+    """A captured forward replays with new frame / output / depth_low buffers (no stale pointers)."""
+    from illumina import _lib
+    m = _model(64, 3, maxBatch=2)
+    a = torch.empty((2, 3, 64, 64), device="cuda")
+    b = torch.empty((2, 3, 64, 64), device="cuda")
+    _lib.check(_lib.lib().illumina_generate_frames(0, 10, 2, 64, a.data_ptr(), None))
+    _lib.check(_lib.lib().illumina_generate_frames(1, 20, 2, 64, b.data_ptr(), None))
+    x, y = torch.full((2, 64, 64), -1.0, device="cuda"), torch.full((2, 64, 64), -1.0, device="cuda")
+    lx, ly = torch.full((2, 32, 32), -1.0, device="cuda"), torch.full((2, 32, 32), -1.0, device="cuda")
+    want_a = m.forward(a.clone()).cpu().numpy()
+    want_b = m.forward(b.clone()).cpu().numpy()
+    for src, dst, low, want in [(a, x, lx, want_a), (b, y, ly, want_b), (a, y, lx, want_a), (b, x, ly, want_b)]:
+        m.forward(src, disparity=dst, depthLow=low)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(dst.cpu().numpy(), want)
+        assert (low.cpu().numpy() >= 0).all()
+    m.destroy()
+
+
 def test_host_and_device_buffers_agree(torch, net64):
     rgb, _, disp = net64
     m = _model(64, cases.NET64_SEED, maxBatch=2)

@@ -128,23 +128,6 @@ def test_flat_plane_normals_and_ggx_peak(torch):
     np.testing.assert_allclose(gh[c, c, :3], [0.5, 0.5, 1.0], atol=1e-6)
 
 
-def test_ggx_and_smith_closed_forms():
-    """brdf.test.ts:57-81 on the float32 shader terms (oracle), |D/D_ref - 1| < 1e-3."""
-    from oracle import lib
-    worst = 0.0
-    for r in [0.04, 0.08, 0.12, 0.155, 0.2, 0.3, 0.55, 1.0]:
-        for nh in [1.0, 0.9999, 0.999, 0.99, 0.9, 0.7, 0.5]:
-            a = r * r
-            a2 = a * a
-            den = nh * nh * (a2 - 1) + 1
-            d_ref = a2 / (math.pi * den * den)
-            k = (r + 1) ** 2 / 8
-            g_ref = (0.8 / (0.8 * (1 - k) + k)) * (0.6 / (0.6 * (1 - k) + k))
-            worst = max(worst, abs(lib().or_ggx_d(nh, r) / d_ref - 1))
-            assert abs(lib().or_smith_g(0.8, 0.6, r) - g_ref) < 1e-6
-    assert worst < 1e-3
-
-
 RANGES = dict(exposure=(0.1, 4), contrast=(0.6, 1.6), saturation=(0, 2), vignette=(0, 1), near=(0.05, 3),
               far=(2, 60), fovY=(20 * math.pi / 180, 110 * math.pi / 180), normalStrength=(0.1, 4),
               ambientIntensity=(0, 2), shadowStrength=(0, 1), contactShadowLength=(0.05, 4), aoStrength=(0, 1),
