@@ -99,6 +99,8 @@ SIGNATURES = {
     "illumina_op_pointwise": (_S, [_V, C.c_long, C.c_int, _V, _V, C.c_int, C.c_int, _V, _V, _V]),
     "illumina_op_dwpw": (_S, [_V, C.c_int, C.c_int, C.c_int, _V, _V, C.c_int, _V, _V, C.c_int, C.c_int,
                               C.c_int, C.c_int, _V, _V, _V]),
+    "illumina_op_dwpw_noalloc": (_S, [_V, C.c_int, C.c_int, C.c_int, _V, _V, C.c_int, _V, _V, C.c_int,
+                                      C.c_int, C.c_int, C.c_int, _V, _V, _V]),
     "illumina_op_conv": (_S, [_V, C.c_int, C.c_int, C.c_int, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int,
                               _V, _V]),
     "illumina_op_lateral": (_S, [_V, C.c_int, C.c_int, _V, C.c_int, _V, _V, C.c_int, C.c_int, _V, _V]),

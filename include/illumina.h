@@ -213,6 +213,31 @@ illumina_status illumina_op_dwpw(const float *src, int in_h, int in_w, int in_c,
                                  int out_c, int k, int stride, int act, const float *res, float *dst,
                                  void *stream);
 
+/* The fused depthwise -> pointwise op of illumina_op_dwpw, for callers that
+ * cannot allocate device memory. It has no counterpart in the reference.
+ *
+ * Why: illumina_op_dwpw obtains a temporary buffer (cudaMallocAsync) to
+ * repack the depthwise weights. Some callers cannot allow that: a real-time
+ * frame loop with a fixed device-memory budget, where an allocation may fail
+ * or wait for memory mid-frame; or a host application whose own memory
+ * manager reserves the device heap up front and forbids plugins from
+ * allocating. This variant repacks into a fixed device array compiled into the
+ * library (ILLUMINA_NOALLOC_DW_MAX_FLOATS floats, 256 KiB, reserved on every
+ * GPU that loads the library until the process exits) and calls no
+ * allocation routine.
+ *
+ * Limit: in_c * k * k must not exceed ILLUMINA_NOALLOC_DW_MAX_FLOATS, else the
+ * call returns ILLUMINA_INVALID_ARG. The first call on a device resolves the
+ * array's device address (cudaGetSymbolAddress) with that device current; make
+ * that first call before any stream capture. All calls share the array: calls
+ * whose GPU work overlaps (other streams or host threads on the same device)
+ * race. Arguments and result are those of illumina_op_dwpw. */
+#define ILLUMINA_NOALLOC_DW_MAX_FLOATS 65536
+illumina_status illumina_op_dwpw_noalloc(const float *src, int in_h, int in_w, int in_c, const float *dw_w,
+                                         const float *dw_b, int mid_act, const float *pw_w, const float *pw_b,
+                                         int out_c, int k, int stride, int act, const float *res, float *dst,
+                                         void *stream);
+
 /* makeConv (kernels/conv.ts:94-168): dense k x k stride s, zero pad, w is
  * [out_c][in_c][k][k]. */
 illumina_status illumina_op_conv(const float *src, int in_h, int in_w, int in_c, const float *w,
