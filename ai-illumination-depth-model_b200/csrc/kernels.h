@@ -53,6 +53,20 @@ struct GemmOp {
 
 cudaError_t gemm(int T, const GemmOp &op, cudaStream_t st);
 
+// Tensor-core (tcgen05) engine for the same ops (tc_gemm.cu). The weights of
+// each op are pre-packed into swizzled per-(n tile, K slab) shared-memory
+// images: tf32 hi/lo pairs for fp32 storage, bf16 for bf16 storage.
+struct TcWeights {
+  int N = 0, K = 0;
+  int n_tile = 0, n_tiles = 0, slabs = 0;  // accumulator columns per CTA, tiles along N, K slabs
+  uint32_t tmem_cols = 0;
+  size_t bytes = 0;                         // size of the packed images
+};
+TcWeights tc_plan(int T, int N, int K);
+cudaError_t tc_pack(int T, const float *w, int N, int K, const TcWeights &plan, uint8_t *out, cudaStream_t st);
+size_t tc_smem_bytes(int T, const TcWeights &plan);
+cudaError_t tc_gemm(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st);
+
 // Head: src (M,C) storage T -> dst1 (M) f32 disparity (1 channel) and/or
 // dst4 (M*4) f32 broadcast.
 cudaError_t head(int T, const void *src, long M, int C, const float *w, float bias, float *dst1, float *dst4,

@@ -123,6 +123,11 @@ struct illumina_model {
   float exposure = 1, range_sigma = 0.12f, base_alpha = 0.35f, sensitivity = 3.0f;
   std::vector<GraphEntry> graphs;
   int launches_per_forward = 0;
+  int engine = ILLUMINA_ENGINE_TENSOR;
+  std::vector<gpu::TcWeights> tcw;   // per op (pw / dwpw / lateral)
+  std::vector<size_t> tc_off;        // per op: byte offset into d_wimg
+  uint8_t *d_wimg = nullptr;         // tensor-core weight images
+  int *d_err = nullptr;              // set by a kernel that gave up a bounded wait
 
   void *tensor(const std::string &name) {
     auto it = plan.assignment.find(name);
@@ -152,6 +157,8 @@ illumina_model::~illumina_model() {
   cudaFree(d_stage_in);
   cudaFree(d_stage_out);
   cudaFree(d_stage_low);
+  cudaFree(d_wimg);
+  cudaFree(d_err);
   if (ev_join) cudaEventDestroy(ev_join);
   if (ev_done) cudaEventDestroy(ev_done);
   if (stream) cudaStreamDestroy(stream);
@@ -256,7 +263,10 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
             g.mode = 0;
           }
         }
-        cuda_check(gpu::gemm(m.T, g, st), op.name.c_str());
+        if (m.engine == ILLUMINA_ENGINE_TENSOR)
+          cuda_check(gpu::tc_gemm(m.T, g, m.tcw[i], m.d_wimg + m.tc_off[i], m.d_err, st), op.name.c_str());
+        else
+          cuda_check(gpu::gemm(m.T, g, st), op.name.c_str());
         launches++;
         break;
       }
@@ -512,6 +522,36 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
     if (op.kind == OpKind::Head) w.head_bias = m.host_weights[by_name[op.name + ".bias"]->offset];
   }
 
+  // --- tensor-core weight images (from the logical weights) ---
+  if (o.gemm_engine != ILLUMINA_ENGINE_TENSOR && o.gemm_engine != ILLUMINA_ENGINE_SIMT)
+    throw Error(ILLUMINA_INVALID_ARG, "createDepthModel: unknown gemm engine " + std::to_string(o.gemm_engine));
+  m.engine = o.gemm_engine;
+  cuda_check(cudaMalloc(&m.d_err, sizeof(int)), "cudaMalloc error flag");
+  cuda_check(cudaMemsetAsync(m.d_err, 0, sizeof(int), m.stream), "clear error flag");
+  m.tcw.resize(m.arch.ops.size());
+  m.tc_off.assign(m.arch.ops.size(), 0);
+  if (m.engine == ILLUMINA_ENGINE_TENSOR) {
+    size_t total_img = 0;
+    std::vector<const WeightSpec *> pw_spec(m.arch.ops.size(), nullptr);
+    for (size_t i = 0; i < m.arch.ops.size(); i++) {
+      const Op &op = m.arch.ops[i];
+      if (op.kind != OpKind::Pw && op.kind != OpKind::Dwpw && op.kind != OpKind::Lateral) continue;
+      pw_spec[i] = by_name[op.name + (op.kind == OpKind::Dwpw ? ".pw_weight" : ".weight")];
+      m.tcw[i] = gpu::tc_plan(m.T, pw_spec[i]->shape[0], pw_spec[i]->shape[1]);
+      m.tc_off[i] = total_img;
+      total_img = align_up(total_img + m.tcw[i].bytes, 1024);
+    }
+    cuda_check(cudaMalloc(&m.d_wimg, total_img), "cudaMalloc weight images");
+    cuda_check(cudaMemsetAsync(m.d_wimg, 0, total_img, m.stream), "clear weight images");
+    m.device_bytes += total_img;
+    for (size_t i = 0; i < m.arch.ops.size(); i++) {
+      if (!pw_spec[i]) continue;
+      cuda_check(gpu::tc_pack(m.T, m.d_weights_logical + pw_spec[i]->offset, m.tcw[i].N, m.tcw[i].K, m.tcw[i],
+                              m.d_wimg + m.tc_off[i], m.stream),
+                 "pack weight images");
+    }
+  }
+
   // --- arena: one allocation, buffers 256-byte aligned, sized for max_batch ---
   const size_t B = (size_t)m.opts.max_batch;
   m.buf_off.resize(m.plan.buffer_sizes.size());
@@ -554,6 +594,23 @@ struct Scratch {
 
 void require(bool ok, const std::string &msg) {
   if (!ok) throw Error(ILLUMINA_INVALID_ARG, msg);
+}
+
+thread_local int g_op_engine = ILLUMINA_ENGINE_SIMT;
+
+// Per-kernel entry points: run `g` (fp32, logical [N][K] weights in g.w) on
+// the calling thread's engine; the tensor-core engine packs its weight images
+// into temporary device memory first.
+void op_gemm(const gpu::GemmOp &g, cudaStream_t st, const char *what) {
+  if (g_op_engine == ILLUMINA_ENGINE_SIMT) {
+    cuda_check(gpu::gemm(gpu::F32, g, st), what);
+    return;
+  }
+  gpu::TcWeights plan = gpu::tc_plan(gpu::F32, g.N, g.K);
+  Scratch img(plan.bytes, st);
+  cuda_check(cudaMemsetAsync(img.p, 0, plan.bytes, st), "clear weight images");
+  cuda_check(gpu::tc_pack(gpu::F32, g.w, g.N, g.K, plan, (uint8_t *)img.p, st), "pack weight images");
+  cuda_check(gpu::tc_gemm(gpu::F32, g, plan, (const uint8_t *)img.p, nullptr, st), what);
 }
 
 }  // namespace
@@ -653,6 +710,7 @@ void illumina_model_options_default(illumina_model_options *o) {
   o->temporal_base = 0.35f;
   o->temporal_sensitivity = 3.0f;
   o->synth_seed = 1;
+  o->gemm_engine = ILLUMINA_ENGINE_TENSOR;
 }
 
 illumina_status illumina_model_create(const illumina_model_options *opts, illumina_model **out) {
@@ -783,6 +841,11 @@ illumina_status illumina_model_stats(const illumina_model *m, illumina_stats *ou
   out->max_batch = m->opts.max_batch;
   out->precision = m->opts.precision;
   out->input_size = m->arch.input_size;
+  out->gemm_engine = m->engine;
+  int flag = 0;
+  cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+  cuda_check(cudaMemcpy(&flag, m->d_err, sizeof(int), cudaMemcpyDeviceToHost), "read error flag");
+  out->device_error = flag;
   return ILLUMINA_OK;
   ILL_CATCH
 }
@@ -824,6 +887,14 @@ illumina_status illumina_model_profile(illumina_model *m, const float *frames, i
 
 // ---- per-kernel entry points -------------------------------------------------
 
+illumina_status illumina_set_op_engine(int engine) {
+  ILL_TRY
+  require(engine == ILLUMINA_ENGINE_TENSOR || engine == ILLUMINA_ENGINE_SIMT, "set_op_engine: unknown engine");
+  g_op_engine = engine;
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
 illumina_status illumina_op_pointwise(const float *src, long pixels, int in_c, const float *w, const float *b,
                                       int out_c, int act, const float *res, float *dst, void *stream) {
   ILL_TRY
@@ -833,7 +904,7 @@ illumina_status illumina_op_pointwise(const float *src, long pixels, int in_c, c
   gpu::GemmOp g;
   g.mode = 0, g.src = src, g.w = w, g.bias = b, g.res = res, g.dst = dst, g.M = pixels, g.N = out_c, g.K = in_c;
   g.act = act;
-  cuda_check(gpu::gemm(gpu::F32, g, (cudaStream_t)stream), "pointwise");
+  op_gemm(g, (cudaStream_t)stream, "pointwise");
   return ILLUMINA_OK;
   ILL_CATCH
 }
@@ -856,7 +927,7 @@ illumina_status illumina_op_dwpw(const float *src, int in_h, int in_w, int in_c,
   g.mode = 1, g.src = src, g.w = pw_w, g.bias = pw_b, g.res = res, g.dst = dst;
   g.H = in_h, g.W = in_w, g.OH = oh, g.OW = ow, g.M = (long)oh * ow, g.N = out_c, g.K = in_c;
   g.act = act, g.mid_act = mid_act, g.ks = k, g.stride = stride, g.dw_w = (const float *)pk.p, g.dw_b = dw_b;
-  cuda_check(gpu::gemm(gpu::F32, g, st), "dwpw");
+  op_gemm(g, st, "dwpw");
   return ILLUMINA_OK;
   ILL_CATCH
 }
@@ -886,7 +957,7 @@ illumina_status illumina_op_lateral(const float *coarse, int ch, int cw, const f
   gpu::GemmOp g;
   g.mode = 2, g.src = skip, g.coarse = coarse, g.w = w, g.bias = b, g.dst = dst;
   g.OH = 2 * ch, g.OW = 2 * cw, g.M = 4L * ch * cw, g.N = out_c, g.K = skip_c, g.act = act;
-  cuda_check(gpu::gemm(gpu::F32, g, (cudaStream_t)stream), "lateral");
+  op_gemm(g, (cudaStream_t)stream, "lateral");
   return ILLUMINA_OK;
   ILL_CATCH
 }

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_PKG_DIR, "libillumina.so")
 OK, INVALID_ARG, BAD_WEIGHTS, ARCH_MISMATCH, CUDA_ERROR, TIMEOUT, NO_DEVICE = range(7)
 PRECISION_F32, PRECISION_BF16 = 0, 1
 FRAME_RGB_PLANAR, FRAME_RGBA_INTERLEAVED = 0, 1
+ENGINE = {"tensor": 0, "simt": 1}
 ACT = {"linear": 0, "relu": 1, "relu6": 2, "hardswish": 3}
 
 
@@ -32,7 +33,7 @@ class ModelOptions(C.Structure):
         ("temporal_base", C.c_float), ("temporal_sensitivity", C.c_float),
         ("keep_intermediates", C.c_int), ("weights", C.POINTER(C.c_float)), ("weights_count", C.c_size_t),
         ("idm_bytes", C.c_void_p), ("idm_len", C.c_size_t), ("idm_path", C.c_char_p),
-        ("synth_seed", C.c_uint32),
+        ("synth_seed", C.c_uint32), ("gemm_engine", C.c_int),
     ]
 
 
@@ -40,7 +41,8 @@ class Stats(C.Structure):
     _fields_ = [
         ("dispatches", C.c_int), ("launches", C.c_int), ("arena_bytes", C.c_size_t),
         ("naive_arena_bytes", C.c_size_t), ("weight_bytes", C.c_size_t), ("device_bytes", C.c_size_t),
-        ("max_batch", C.c_int), ("precision", C.c_int), ("input_size", C.c_int),
+        ("max_batch", C.c_int), ("precision", C.c_int), ("input_size", C.c_int), ("gemm_engine", C.c_int),
+        ("device_error", C.c_int),
     ]
 
 
@@ -96,6 +98,7 @@ SIGNATURES = {
                                          C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "illumina_model_stats": (_S, [_V, C.POINTER(Stats)]),
     "illumina_model_profile": (_S, [_V, _V, C.c_int, C.c_int, C.c_int, _V, C.c_int]),
+    "illumina_set_op_engine": (_S, [C.c_int]),
     "illumina_op_pointwise": (_S, [_V, C.c_long, C.c_int, _V, _V, C.c_int, C.c_int, _V, _V, _V]),
     "illumina_op_dwpw": (_S, [_V, C.c_int, C.c_int, C.c_int, _V, _V, C.c_int, _V, _V, C.c_int, C.c_int,
                               C.c_int, C.c_int, _V, _V, _V]),

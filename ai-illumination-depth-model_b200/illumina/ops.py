@@ -6,7 +6,12 @@ same CUDA kernel the model uses.
 """
 from __future__ import annotations
 
-from ._lib import ACT, check, lib, ptr, stream_handle
+from ._lib import ACT, ENGINE, check, lib, ptr, stream_handle
+
+
+def set_engine(engine: str) -> None:
+    """Engine of this thread's pointwise / dw->pw / lateral entry points: "simt" (default) or "tensor"."""
+    check(lib().illumina_set_op_engine(ENGINE[engine]))
 
 
 def _out(torch, shape, like):

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import (FRAME_RGB_PLANAR, FRAME_RGBA_INTERLEAVED, PRECISION_BF16, PRECISION_F32, ModelOptions, Stats,
+from ._lib import (ENGINE, FRAME_RGB_PLANAR, FRAME_RGBA_INTERLEAVED, PRECISION_BF16, PRECISION_F32, ModelOptions, Stats,
                    check, lib, ptr, stream_handle)
 from .arch import Architecture, buildArchitecture
 from .weights import flatten
@@ -38,6 +38,8 @@ class DepthModelStats:
     maxBatch: int
     precision: str
     inputSize: int
+    engine: str
+    deviceError: int
 
 
 def _is_torch(x) -> bool:
@@ -131,7 +133,7 @@ class DepthModel:
         check(lib().illumina_model_stats(self._h, C.byref(s)))
         return DepthModelStats(s.dispatches, s.launches, s.arena_bytes, s.naive_arena_bytes, s.weight_bytes,
                                s.device_bytes, s.max_batch, "bf16" if s.precision == PRECISION_BF16 else "f32",
-                               s.input_size)
+                               s.input_size, "tensor" if s.gemm_engine == 0 else "simt", s.device_error)
 
     def profile(self, frames, reps: int = 3):
         """Per-op mean device time in ms (GpuProfiler analogue), frames on the device."""
@@ -167,11 +169,12 @@ def createDepthModel(arch: Architecture | None = None, weights: dict | None = No
                      decodeSrgb: bool = True, exposure: float = 1.0, device: int = 0, maxBatch: int = 1,
                      precision: str = "f32", keepIntermediates: bool = False, synthSeed: int = 1,
                      rangeSigma: float = 0.12, temporalBase: float = 0.35,
-                     temporalSensitivity: float = 3.0) -> DepthModel:
+                     temporalSensitivity: float = 3.0, engine: str = "tensor") -> DepthModel:
     """createDepthModel (runner.ts:160-485).
 
     Weights: a WeightMap (`weights`), or an .idm container (`idm`), else the
     seeded Kaiming fallback synthesizeWeights(arch, synthSeed) (main.ts:61).
+    `engine` selects the pointwise-shaped ops' engine: "tensor" (tcgen05) or "simt".
     """
     arch = arch or buildArchitecture(448)
     o = ModelOptions()
@@ -187,6 +190,7 @@ def createDepthModel(arch: Architecture | None = None, weights: dict | None = No
     o.temporal_sensitivity = temporalSensitivity
     o.keep_intermediates = 1 if keepIntermediates else 0
     o.synth_seed = synthSeed & 0xFFFFFFFF
+    o.gemm_engine = ENGINE[engine]
     keep = []
     if weights is not None:
         blob = flatten(arch, weights)

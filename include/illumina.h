@@ -124,7 +124,13 @@ typedef struct illumina_model_options {
   size_t idm_len;
   const char *idm_path;
   uint32_t synth_seed;
+  int gemm_engine;         /* ILLUMINA_ENGINE_* for the pw / dw->pw / lateral ops */
 } illumina_model_options;
+
+/* Engines for the pointwise-shaped ops: tcgen05 tensor cores with TMEM
+ * accumulators (fp32 storage: 3xTF32 split products; bf16: kind::f16), or the
+ * CUDA-core register-blocked tile GEMM. */
+enum { ILLUMINA_ENGINE_TENSOR = 0, ILLUMINA_ENGINE_SIMT = 1 };
 
 /* Defaults: 448, device 0, batch 1, fp32, sRGB on, exposure 1, (0.12, 0.35,
  * 3.0), aliased arena, synthetic seed 1. */
@@ -183,6 +189,8 @@ typedef struct illumina_stats {
   int max_batch;
   int precision;
   int input_size;
+  int gemm_engine;         /* ILLUMINA_ENGINE_* */
+  int device_error;        /* non-zero: a kernel gave up a bounded wait (reads a device flag; synchronises) */
 } illumina_stats;
 illumina_status illumina_model_stats(const illumina_model *model, illumina_stats *out);
 
@@ -199,6 +207,11 @@ illumina_status illumina_model_profile(illumina_model *model, const float *frame
  * Per-kernel entry points (the kernel factories under src/model/kernels/).
  * All pointers are device pointers; weights are in the logical .idm layout.
  * ------------------------------------------------------------------------- */
+
+/* Selects, for the calling thread, the engine the per-kernel entry points
+ * below use for pointwise / dw->pw / lateral (ILLUMINA_ENGINE_*; default
+ * SIMT). No reference counterpart: the reference has one WGSL kernel per op. */
+illumina_status illumina_set_op_engine(int engine);
 
 /* makePointwise (kernels/pointwise.ts:64-133): dst[p][oc] = act(b[oc] +
  * sum_ic w[oc][ic]*src[p][ic] (+ res[p][oc])). */

@@ -57,11 +57,20 @@ def run_case(torch, case, data, guard=0):
     return out[:n], out[n:]
 
 
+@pytest.mark.parametrize("engine", ["simt", "tensor"])
 @pytest.mark.parametrize("case", cases.all_cases(), ids=lambda c: c["id"])
-def test_kernel_matches_oracle(torch, case):
+def test_kernel_matches_oracle(torch, case, engine):
+    """Every case on both engines; the tensor engine (tcgen05, 3xTF32) meets the same tolerances."""
+    from illumina import ops
+    if engine == "tensor" and case["kind"] == "conv":
+        pytest.skip("the stem conv has one engine")
     data = cases.draw(case)
     want = cases.oracle_output(case, data)
-    got, tail = run_case(torch, case, data, guard=64)
+    ops.set_engine(engine)
+    try:
+        got, tail = run_case(torch, case, data, guard=64)
+    finally:
+        ops.set_engine("simt")
     max_abs, max_rel, worst = compare(got, want, *case["tol"])
     assert worst == [], f"maxAbs={max_abs:.3e} maxRel={max_rel:.3e} worst={worst}"
     assert (tail == -98765.0).all(), "kernel wrote past the end of its output"

@@ -51,9 +51,11 @@ def _model(size, seed, **kw):
     return illumina.createDepthModel(illumina.buildArchitecture(size), synthSeed=seed, **kw)
 
 
-def test_network64_every_layer_fp32(torch, net64):
+@pytest.mark.parametrize("engine", ["tensor", "simt"])
+def test_network64_every_layer_fp32(torch, net64, engine):
     rgb, values, disp = net64
-    m = _model(64, cases.NET64_SEED, keepIntermediates=True)
+    m = _model(64, cases.NET64_SEED, keepIntermediates=True, engine=engine)
+    assert m.stats.engine == engine
     low = np.empty((1, 32, 32), np.float32)
     got = m.forward(rgb[None], depthLow=low)
     for name, want in values.items():
@@ -93,7 +95,7 @@ def test_network64_aliased_arena_live_at_end(torch, net64):
     _, live_in = m.debugTensor("input")
     assert not live_in  # the arena recycles `input` right after the stem (network.test.ts:81-84)
     s = m.stats
-    assert s.dispatches == 40 and s.launches == 40
+    assert s.dispatches == 40 and s.launches == 40 and s.deviceError == 0
     assert abs(s.arenaBytes - 19.03e6 / 49) < 1e5 or s.arenaBytes < s.naiveArenaBytes
     m.destroy()
 
