@@ -3,7 +3,8 @@ forward), against the CPU oracle on the same seeded weights and inputs.
 
 Tolerances (stated here, checked per layer, scale-relative because the
 untrained seeded network grows activations to ~1e4 by the bottleneck):
-  fp32: every conv output max|got-want|/max|want| <= 2e-5 and rel-L2 <= 5e-6;
+  fp32 (both engines; the tensor engine is 3xTF32): every conv output
+        max|got-want|/max|want| <= 1e-4 and rel-L2 <= 5e-5;
         final disparity and depth_low max-abs <= 2e-4 (the head's logits reach
         O(100) at 448, so an fp32 logit error of a few 1e-4 reaches the sigmoid
         output near its steep middle).
@@ -21,7 +22,7 @@ from tests.helpers import compare, scale_metrics
 
 pytestmark = pytest.mark.gpu
 
-FP32_MAXREL, FP32_L2, FP32_DISP = 2e-5, 5e-6, 2e-4
+FP32_MAXREL, FP32_L2, FP32_DISP = 1e-4, 5e-5, 2e-4
 BF16_L2, BF16_DISP_MAX, BF16_DISP_MEAN = 3e-2, 3e-2, 3e-3
 
 
