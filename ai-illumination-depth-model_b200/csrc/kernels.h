@@ -66,6 +66,16 @@ TcWeights tc_plan(int T, int N, int K);
 cudaError_t tc_pack(int T, const float *w, int N, int K, const TcWeights &plan, uint8_t *out, cudaStream_t st);
 size_t tc_smem_bytes(int T, const TcWeights &plan);
 cudaError_t tc_gemm(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st);
+// Persistent warp-specialised variant for pointwise (mode 0) and lateral
+// (mode 2): TMA A tiles, bulk-copied weight images, double-buffered TMEM
+// accumulators (tc_pw.cu). Same weight images as tc_gemm.
+cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st);
+
+// Tensor-core dispatch: pointwise / lateral on tc_pw, depthwise->pointwise on tc_gemm.
+inline cudaError_t tc_op(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err,
+                         cudaStream_t st) {
+  return op.mode == 1 ? tc_gemm(T, op, plan, wimg, err, st) : tc_pw(T, op, plan, wimg, err, st);
+}
 
 // Head: src (M,C) storage T -> dst1 (M) f32 disparity (1 channel) and/or
 // dst4 (M*4) f32 broadcast.

@@ -264,7 +264,7 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
           }
         }
         if (m.engine == ILLUMINA_ENGINE_TENSOR)
-          cuda_check(gpu::tc_gemm(m.T, g, m.tcw[i], m.d_wimg + m.tc_off[i], m.d_err, st), op.name.c_str());
+          cuda_check(gpu::tc_op(m.T, g, m.tcw[i], m.d_wimg + m.tc_off[i], m.d_err, st), op.name.c_str());
         else
           cuda_check(gpu::gemm(m.T, g, st), op.name.c_str());
         launches++;
@@ -610,7 +610,7 @@ void op_gemm(const gpu::GemmOp &g, cudaStream_t st, const char *what) {
   Scratch img(plan.bytes, st);
   cuda_check(cudaMemsetAsync(img.p, 0, plan.bytes, st), "clear weight images");
   cuda_check(gpu::tc_pack(gpu::F32, g.w, g.N, g.K, plan, (uint8_t *)img.p, st), "pack weight images");
-  cuda_check(gpu::tc_gemm(gpu::F32, g, plan, (const uint8_t *)img.p, nullptr, st), what);
+  cuda_check(gpu::tc_op(gpu::F32, g, plan, (const uint8_t *)img.p, nullptr, st), what);
 }
 
 }  // namespace
