@@ -1,0 +1,257 @@
+// Shared pieces of the persistent tcgen05 kernels (tc_pw.cu, tc_dw.cu):
+// PTX wrappers for mbarriers, TMA, TMEM and UMMA, and the accumulator
+// epilogue.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace illumina {
+namespace gpu {
+namespace tcx {
+
+constexpr int kTileM = 128;
+constexpr uint32_t kAImage = kTileM * 128;  // one 128-row x 128-byte operand image
+constexpr long long kWaitCycles = 1ll << 31;
+constexpr int kEpiWarps = 8;                // 2 per TMEM lane quarter (column halves)
+constexpr int kEpiCols = 16;                // accumulator columns per transpose block
+constexpr int kEpiStride = 20;              // floats per row of a block (16 + 4 pad: conflict-free)
+constexpr uint32_t kEpiSmem = kEpiWarps * 32 * kEpiStride * 4;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of parity `parity`; false once ~2^31 cycles pass.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > kWaitCycles) return false;
+  return true;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms
+// 1024 bytes apart (SBO), LBO unused, descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: D fp32, A/B format (1 bf16, 2 tf32), K-major, M = 128.
+__host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_format, uint32_t n) {
+  return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((n >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// One 128-byte slab of K for a 128 x N tile: 4 MMAs of K = 32 bytes; fp32
+// storage issues the 4 TF32 cross products of the hi/lo split (small terms first).
+template <bool F32>
+__device__ __forceinline__ void mma_slab(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
+                                         uint32_t idesc, bool first) {
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    const uint32_t ko = kk * 32;
+    const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+    if (F32) {
+      mma_tf32(d, smem_desc(a_lo + ko), smem_desc(b_lo + ko), idesc, acc);
+      mma_tf32(d, smem_desc(a_lo + ko), smem_desc(b_hi + ko), idesc, 1u);
+      mma_tf32(d, smem_desc(a_hi + ko), smem_desc(b_lo + ko), idesc, 1u);
+      mma_tf32(d, smem_desc(a_hi + ko), smem_desc(b_hi + ko), idesc, 1u);
+    } else {
+      mma_f16(d, smem_desc(a_hi + ko), smem_desc(b_hi + ko), idesc, acc);
+    }
+  }
+}
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t r[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+// x = hi + lo with hi, lo exact TF32 values, both rounded to nearest.
+__device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ float act_apply(int act, float v) {
+  switch (act) {
+    case 1: return fmaxf(v, 0.0f);
+    case 2: return fminf(fmaxf(v, 0.0f), 6.0f);
+    case 3: return (v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)) / 6.0f;
+    default: return v;
+  }
+}
+__device__ __forceinline__ float4 act4(int act, float4 v) {
+  return make_float4(act_apply(act, v.x), act_apply(act, v.y), act_apply(act, v.z), act_apply(act, v.w));
+}
+__device__ __forceinline__ float4 ld4(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16 *p) {
+  uint2 r = __ldg(reinterpret_cast<const uint2 *>(p));
+  float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&r.x));
+  float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&r.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+__device__ __forceinline__ void st4(__nv_bfloat16 *p, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 r;
+  r.x = *reinterpret_cast<uint32_t *>(&a);
+  r.y = *reinterpret_cast<uint32_t *>(&b);
+  *reinterpret_cast<uint2 *>(p) = r;
+}
+__device__ __forceinline__ float4 f4fma(float4 a, float4 b, float4 c) {
+  return make_float4(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y), fmaf(a.z, b.z, c.z), fmaf(a.w, b.w, c.w));
+}
+
+struct EpiArgs {
+  const float *bias;
+  const void *res;     // [M][N] or null
+  const void *coarse;  // lateral: (n, OH/2, OW/2, N) or null
+  void *dst;           // [M][N]
+  int N, act, OH, OW;
+  int n_tile;
+};
+
+// Writes accumulator columns [col0, col0 + ncols) of the 32 TMEM lanes this
+// warp owns. `pix(r)` maps a tile row (0..127) to its output pixel, or -1 for
+// a padding row. Each 16-column block is read with back-to-back tcgen05.ld,
+// transposed through this warp's shared block so that every store
+// instruction writes eight 64-byte row segments (whole sectors), then
+// biased, residual/coarse-added, activated and stored. The tcgen05.ld
+// issue count depends only on warp-uniform values.
+template <typename T, int MODE, typename PixFn>
+__device__ __forceinline__ void epilogue_rows(const EpiArgs &a, uint32_t tacc_lane, int lane_base, int col0, int ncols,
+                                              int n_base, float *blk, PixFn pix) {
+  const int lane = threadIdx.x & 31;
+  const T *res = reinterpret_cast<const T *>(a.res);
+  const T *coarse = reinterpret_cast<const T *>(a.coarse);
+  T *dst = reinterpret_cast<T *>(a.dst);
+  for (int cb = 0; cb < ncols; cb += kEpiCols) {
+    const int width = min(kEpiCols, ncols - cb);  // 8 or 16, warp-uniform
+    uint32_t v[kEpiCols];
+    tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb), v);
+    if (width > 8) tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb + 8), v + 8);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < kEpiCols / 4; j++)
+      if (j * 4 < width)
+        *reinterpret_cast<float4 *>(blk + lane * kEpiStride + j * 4) =
+            make_float4(__uint_as_float(v[j * 4]), __uint_as_float(v[j * 4 + 1]), __uint_as_float(v[j * 4 + 2]),
+                        __uint_as_float(v[j * 4 + 3]));
+    __syncwarp();
+    const int chunk = lane & 3;
+    const int n = n_base + col0 + cb + chunk * 4;
+    const bool col_ok = chunk * 4 < width && n < a.N;
+    float4 bias = make_float4(0, 0, 0, 0);
+    if (col_ok) bias = __ldg(reinterpret_cast<const float4 *>(a.bias + n));
+#pragma unroll 2
+    for (int i = 0; i < 4; i++) {
+      const int row = i * 8 + (lane >> 2);
+      const long m = pix(lane_base + row);
+      if (!col_ok || m < 0) continue;
+      float4 o = *reinterpret_cast<const float4 *>(blk + row * kEpiStride + chunk * 4);
+      o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
+      if (MODE == 2) {
+        // refUpsample2 taps (reference.ts:161-193): (i + 0.5) / 2 - 0.5, both
+        // taps from the unclamped floor, clamped independently
+        const int x = (int)(m % a.OW);
+        const long t = m / a.OW;
+        const int y = (int)(t % a.OH), b = (int)(t / a.OH);
+        const int CH = a.OH >> 1, CW = a.OW >> 1;
+        const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
+        const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
+        const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
+        const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
+        const long r0 = ((long)b * CH + y0) * CW, r1 = ((long)b * CH + y1) * CW;
+        const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
+        const float4 c00 = ld4(coarse + (r0 + x0) * a.N + n), c01 = ld4(coarse + (r0 + x1) * a.N + n);
+        const float4 c10 = ld4(coarse + (r1 + x0) * a.N + n), c11 = ld4(coarse + (r1 + x1) * a.N + n);
+        o.x += c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
+        o.y += c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
+        o.z += c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
+        o.w += c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
+      }
+      if (res) {
+        const float4 q = ld4(res + m * a.N + n);
+        o.x += q.x, o.y += q.y, o.z += q.z, o.w += q.w;
+      }
+      st4(dst + m * a.N + n, act4(a.act, o));
+    }
+    __syncwarp();
+  }
+}
+
+}  // namespace tcx
+}  // namespace gpu
+}  // namespace illumina

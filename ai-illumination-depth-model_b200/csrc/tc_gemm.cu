@@ -441,7 +441,9 @@ TcWeights tc_plan(int T, int N, int K) {
   w.N = N, w.K = K;
   const int slab_c = T == F32 ? 32 : 64;
   w.slabs = (K + slab_c - 1) / slab_c;
-  int tiles = (N + 255) / 256;
+  // at most 240 accumulator columns per tile: two fp32 ring stages of a wider
+  // tile no longer fit beside the epilogue's shared-memory buffer
+  int tiles = (N + 239) / 240;
   int per = (N + tiles - 1) / tiles;
   w.n_tile = (per + 15) / 16 * 16;
   w.n_tiles = (N + w.n_tile - 1) / w.n_tile;
