@@ -61,6 +61,8 @@ struct TcWeights {
   int n_tile = 0, n_tiles = 0, slabs = 0;  // accumulator columns per CTA, tiles along N, K slabs
   uint32_t tmem_cols = 0;
   size_t bytes = 0;                         // size of the packed images
+  int ks = 0;                               // depthwise kernel size (dw->pw ops)
+  size_t dw_off = 0, dw_bytes = 0;          // depthwise slab blocks after the images
 };
 TcWeights tc_plan(int T, int N, int K);
 cudaError_t tc_pack(int T, const float *w, int N, int K, const TcWeights &plan, uint8_t *out, cudaStream_t st);
@@ -71,10 +73,19 @@ cudaError_t tc_gemm(int T, const GemmOp &op, const TcWeights &plan, const uint8_
 // accumulators (tc_pw.cu). Same weight images as tc_gemm.
 cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st);
 
-// Tensor-core dispatch: pointwise / lateral on tc_pw, depthwise->pointwise on tc_gemm.
+// Depthwise->pointwise (mode 1) on the persistent kernel of tc_dw.cu: the
+// plan adds per-slab depthwise weight blocks ([slab][ks*ks + 1][slab_c] f32,
+// taps then bias) after the pointwise images; tc_pack_dw fills them from the
+// packed [ks*ks][K] taps and the [K] bias.
+TcWeights tc_plan_dw(int T, int N, int K, int ks);
+cudaError_t tc_pack_dw(int T, const float *dw_w, const float *dw_b, const TcWeights &plan, uint8_t *out,
+                       cudaStream_t st);
+cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st);
+
+// Tensor-core dispatch: pointwise / lateral on tc_pw, depthwise->pointwise on tc_dw.
 inline cudaError_t tc_op(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err,
                          cudaStream_t st) {
-  return op.mode == 1 ? tc_gemm(T, op, plan, wimg, err, st) : tc_pw(T, op, plan, wimg, err, st);
+  return op.mode == 1 ? tc_dw(T, op, plan, wimg, err, st) : tc_pw(T, op, plan, wimg, err, st);
 }
 
 // Head: src (M,C) storage T -> dst1 (M) f32 disparity (1 channel) and/or

@@ -537,7 +537,8 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
       const Op &op = m.arch.ops[i];
       if (op.kind != OpKind::Pw && op.kind != OpKind::Dwpw && op.kind != OpKind::Lateral) continue;
       pw_spec[i] = by_name[op.name + (op.kind == OpKind::Dwpw ? ".pw_weight" : ".weight")];
-      m.tcw[i] = gpu::tc_plan(m.T, pw_spec[i]->shape[0], pw_spec[i]->shape[1]);
+      m.tcw[i] = op.kind == OpKind::Dwpw ? gpu::tc_plan_dw(m.T, pw_spec[i]->shape[0], pw_spec[i]->shape[1], op.k)
+                                         : gpu::tc_plan(m.T, pw_spec[i]->shape[0], pw_spec[i]->shape[1]);
       m.tc_off[i] = total_img;
       total_img = align_up(total_img + m.tcw[i].bytes, 1024);
     }
@@ -549,6 +550,9 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
       cuda_check(gpu::tc_pack(m.T, m.d_weights_logical + pw_spec[i]->offset, m.tcw[i].N, m.tcw[i].K, m.tcw[i],
                               m.d_wimg + m.tc_off[i], m.stream),
                  "pack weight images");
+      if (m.tcw[i].dw_bytes)
+        cuda_check(gpu::tc_pack_dw(m.T, m.opw[i].dw_w, m.opw[i].dw_b, m.tcw[i], m.d_wimg + m.tc_off[i], m.stream),
+                   "pack depthwise blocks");
     }
   }
 
@@ -606,10 +610,12 @@ void op_gemm(const gpu::GemmOp &g, cudaStream_t st, const char *what) {
     cuda_check(gpu::gemm(gpu::F32, g, st), what);
     return;
   }
-  gpu::TcWeights plan = gpu::tc_plan(gpu::F32, g.N, g.K);
+  gpu::TcWeights plan = g.mode == 1 ? gpu::tc_plan_dw(gpu::F32, g.N, g.K, g.ks) : gpu::tc_plan(gpu::F32, g.N, g.K);
   Scratch img(plan.bytes, st);
   cuda_check(cudaMemsetAsync(img.p, 0, plan.bytes, st), "clear weight images");
   cuda_check(gpu::tc_pack(gpu::F32, g.w, g.N, g.K, plan, (uint8_t *)img.p, st), "pack weight images");
+  if (g.mode == 1)
+    cuda_check(gpu::tc_pack_dw(gpu::F32, g.dw_w, g.dw_b, plan, (uint8_t *)img.p, st), "pack depthwise blocks");
   cuda_check(gpu::tc_op(gpu::F32, g, plan, (const uint8_t *)img.p, nullptr, st), what);
 }
 

@@ -139,18 +139,54 @@ __device__ __forceinline__ uint32_t tf32_rna(float x) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
 }
+// Round-to-nearest, ties away from zero, to TF32 (10 explicit mantissa bits)
+// with two integer operations: adding half of the dropped range to the
+// magnitude bits carries into the kept bits (and the exponent) exactly when
+// the dropped part is at least one half ulp. illumina_selftest compares it
+// with cvt.rna.tf32.f32 over every non-NaN binary32 input.
+__device__ __forceinline__ uint32_t tf32_round(float x) { return (__float_as_uint(x) + 0x1000u) & 0xffffe000u; }
 // x = hi + lo with hi, lo exact TF32 values, both rounded to nearest.
 __device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
-  hi = tf32_rna(x);
-  lo = tf32_rna(x - __uint_as_float(hi));
+  hi = tf32_round(x);
+  lo = tf32_round(x - __uint_as_float(hi));
 }
+// a / 6 rounded to nearest, by the quotient-by-a-known-divisor method of
+// Brisebarre, Muller and Raina ("Accelerating correctly rounded
+// floating-point division when the divisor is known in advance", IEEE Trans.
+// Computers 53(8), 2004): q = RN(a * RN(1/6)), r = a - q * 6 (exact, one FMA),
+// q' = RN(q + r * RN(1/6)). The method assumes normal intermediates, so
+// inputs below 2^-100 (quotients near the subnormal range) take the IEEE
+// division, and infinities pass through unchanged. illumina_selftest compares
+// the result bit for bit with a / 6.0f over every non-NaN binary32 input.
+__device__ __forceinline__ float div6(float a) {
+  if (fabsf(a) < 7.8886091e-31f) return a / 6.0f;  // 2^-100
+  const float c = 0.16666667f;
+  const float q = a * c;
+  const float r = fmaf(-q, 6.0f, a);
+  const float q1 = fmaf(r, c, q);
+  return isinf(q) ? q : q1;
+}
+__device__ __forceinline__ float hardswish(float v) { return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)); }
 __device__ __forceinline__ float act_apply(int act, float v) {
   switch (act) {
     case 1: return fmaxf(v, 0.0f);
     case 2: return fminf(fmaxf(v, 0.0f), 6.0f);
-    case 3: return (v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)) / 6.0f;
+    case 3: return hardswish(v);
     default: return v;
   }
+}
+// Compile-time activation (0 linear, 1 relu, 2 relu6, 3 hardswish) for loops
+// that dispatch on the activation once, outside the loop.
+template <int ACT>
+__device__ __forceinline__ float act_c(float v) {
+  if (ACT == 1) return fmaxf(v, 0.0f);
+  if (ACT == 2) return fminf(fmaxf(v, 0.0f), 6.0f);
+  if (ACT == 3) return hardswish(v);
+  return v;
+}
+template <int ACT>
+__device__ __forceinline__ float4 act_c4(float4 v) {
+  return make_float4(act_c<ACT>(v.x), act_c<ACT>(v.y), act_c<ACT>(v.z), act_c<ACT>(v.w));
 }
 __device__ __forceinline__ float4 act4(int act, float4 v) {
   return make_float4(act_apply(act, v.x), act_apply(act, v.y), act_apply(act, v.z), act_apply(act, v.w));
@@ -184,24 +220,49 @@ struct EpiArgs {
 };
 
 // Writes accumulator columns [col0, col0 + ncols) of the 32 TMEM lanes this
-// warp owns. `pix(r)` maps a tile row (0..127) to its output pixel, or -1 for
-// a padding row. Each 16-column block is read with back-to-back tcgen05.ld,
+// warp owns. Lane l handles rows i*8 + l/4 (i < 4) of the warp's 32 and
+// column chunk l%4 of every 16-column block; m[i] is that row's output pixel
+// (-1 for a padding row). Each block is read with back-to-back tcgen05.ld,
 // transposed through this warp's shared block so that every store
 // instruction writes eight 64-byte row segments (whole sectors), then
-// biased, residual/coarse-added, activated and stored. The tcgen05.ld
+// biased, residual/coarse-added, activated and stored. The residual of the
+// next block is loaded while the current one is processed. The tcgen05.ld
 // issue count depends only on warp-uniform values.
-template <typename T, int MODE, typename PixFn>
-__device__ __forceinline__ void epilogue_rows(const EpiArgs &a, uint32_t tacc_lane, int lane_base, int col0, int ncols,
-                                              int n_base, float *blk, PixFn pix) {
-  const int lane = threadIdx.x & 31;
+template <typename T, int MODE, int ACT>
+__device__ __forceinline__ void epilogue_body(const EpiArgs &a, uint32_t tacc_lane, int col0, int ncols, int n_base,
+                                              float *blk, const long (&m)[4]) {
+  const int lane = threadIdx.x & 31, chunk = lane & 3, rsub = lane >> 2;
   const T *res = reinterpret_cast<const T *>(a.res);
   const T *coarse = reinterpret_cast<const T *>(a.coarse);
   T *dst = reinterpret_cast<T *>(a.dst);
+  const long m0 = m[0], m1 = m[1], m2 = m[2], m3 = m[3];
+  const float4 z = make_float4(0, 0, 0, 0);
+  float4 r0 = z, r1 = z, r2 = z, r3 = z;  // residual of the current block
+  if (MODE != 2 && res && chunk * 4 < ncols) {
+    const int n = n_base + col0 + chunk * 4;
+    if (n < a.N) {
+      if (m0 >= 0) r0 = ld4(res + m0 * a.N + n);
+      if (m1 >= 0) r1 = ld4(res + m1 * a.N + n);
+      if (m2 >= 0) r2 = ld4(res + m2 * a.N + n);
+      if (m3 >= 0) r3 = ld4(res + m3 * a.N + n);
+    }
+  }
   for (int cb = 0; cb < ncols; cb += kEpiCols) {
     const int width = min(kEpiCols, ncols - cb);  // 8 or 16, warp-uniform
     uint32_t v[kEpiCols];
     tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb), v);
     if (width > 8) tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb + 8), v + 8);
+    // residual of the next block, in flight while this one is processed
+    float4 q0 = z, q1 = z, q2 = z, q3 = z;
+    if (MODE != 2 && res && chunk * 4 < ncols - cb - kEpiCols) {
+      const int n = n_base + col0 + cb + kEpiCols + chunk * 4;
+      if (n < a.N) {
+        if (m0 >= 0) q0 = ld4(res + m0 * a.N + n);
+        if (m1 >= 0) q1 = ld4(res + m1 * a.N + n);
+        if (m2 >= 0) q2 = ld4(res + m2 * a.N + n);
+        if (m3 >= 0) q3 = ld4(res + m3 * a.N + n);
+      }
+    }
     tmem_wait_ld();
 #pragma unroll
     for (int j = 0; j < kEpiCols / 4; j++)
@@ -210,45 +271,72 @@ __device__ __forceinline__ void epilogue_rows(const EpiArgs &a, uint32_t tacc_la
             make_float4(__uint_as_float(v[j * 4]), __uint_as_float(v[j * 4 + 1]), __uint_as_float(v[j * 4 + 2]),
                         __uint_as_float(v[j * 4 + 3]));
     __syncwarp();
-    const int chunk = lane & 3;
     const int n = n_base + col0 + cb + chunk * 4;
     const bool col_ok = chunk * 4 < width && n < a.N;
-    float4 bias = make_float4(0, 0, 0, 0);
+    float4 bias = z;
     if (col_ok) bias = __ldg(reinterpret_cast<const float4 *>(a.bias + n));
-#pragma unroll 2
-    for (int i = 0; i < 4; i++) {
-      const int row = i * 8 + (lane >> 2);
-      const long m = pix(lane_base + row);
-      if (!col_ok || m < 0) continue;
-      float4 o = *reinterpret_cast<const float4 *>(blk + row * kEpiStride + chunk * 4);
-      o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
-      if (MODE == 2) {
+    if (MODE == 2) {
+#pragma unroll 1
+      for (int i = 0; i < 4; i++) {
+        const long mm = m[i];
+        if (!col_ok || mm < 0) continue;
+        float4 o = *reinterpret_cast<const float4 *>(blk + (i * 8 + rsub) * kEpiStride + chunk * 4);
+        o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
         // refUpsample2 taps (reference.ts:161-193): (i + 0.5) / 2 - 0.5, both
         // taps from the unclamped floor, clamped independently
-        const int x = (int)(m % a.OW);
-        const long t = m / a.OW;
+        const int x = (int)(mm % a.OW);
+        const long t = mm / a.OW;
         const int y = (int)(t % a.OH), b = (int)(t / a.OH);
         const int CH = a.OH >> 1, CW = a.OW >> 1;
         const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
         const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
         const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
         const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
-        const long r0 = ((long)b * CH + y0) * CW, r1 = ((long)b * CH + y1) * CW;
+        const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
         const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
-        const float4 c00 = ld4(coarse + (r0 + x0) * a.N + n), c01 = ld4(coarse + (r0 + x1) * a.N + n);
-        const float4 c10 = ld4(coarse + (r1 + x0) * a.N + n), c11 = ld4(coarse + (r1 + x1) * a.N + n);
+        const float4 c00 = ld4(coarse + (rr0 + x0) * a.N + n), c01 = ld4(coarse + (rr0 + x1) * a.N + n);
+        const float4 c10 = ld4(coarse + (rr1 + x0) * a.N + n), c11 = ld4(coarse + (rr1 + x1) * a.N + n);
         o.x += c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
         o.y += c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
         o.z += c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
         o.w += c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
+        if (res) {
+          const float4 q = ld4(res + mm * a.N + n);
+          o.x += q.x, o.y += q.y, o.z += q.z, o.w += q.w;
+        }
+        st4(dst + mm * a.N + n, act_c4<ACT>(o));
       }
-      if (res) {
-        const float4 q = ld4(res + m * a.N + n);
-        o.x += q.x, o.y += q.y, o.z += q.z, o.w += q.w;
+    } else if (col_ok) {
+      const float4 rr[4] = {r0, r1, r2, r3};
+      const long mr[4] = {m0, m1, m2, m3};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        if (mr[i] < 0) continue;
+        float4 o = *reinterpret_cast<const float4 *>(blk + (i * 8 + rsub) * kEpiStride + chunk * 4);
+        o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
+        o.x += rr[i].x, o.y += rr[i].y, o.z += rr[i].z, o.w += rr[i].w;
+        st4(dst + mr[i] * a.N + n, act_c4<ACT>(o));
       }
-      st4(dst + m * a.N + n, act4(a.act, o));
     }
     __syncwarp();
+    r0 = q0, r1 = q1, r2 = q2, r3 = q3;
+  }
+}
+
+// `pix(r)` maps a tile row (0..127) to its output pixel, or -1 for a padding
+// row; `lane_base` is the first of the warp's 32 TMEM lanes.
+template <typename T, int MODE, typename PixFn>
+__device__ __forceinline__ void epilogue_rows(const EpiArgs &a, uint32_t tacc_lane, int lane_base, int col0, int ncols,
+                                              int n_base, float *blk, PixFn pix) {
+  const int rsub = (threadIdx.x & 31) >> 2;
+  long m[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) m[i] = pix(lane_base + i * 8 + rsub);
+  switch (a.act) {
+    case 1: epilogue_body<T, MODE, 1>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
+    case 2: epilogue_body<T, MODE, 2>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
+    case 3: epilogue_body<T, MODE, 3>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
+    default: epilogue_body<T, MODE, 0>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
   }
 }
 

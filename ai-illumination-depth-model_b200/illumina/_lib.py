@@ -104,6 +104,7 @@ SIGNATURES = {
                               C.c_int, C.c_int, _V, _V, _V]),
     "illumina_op_dwpw_noalloc": (_S, [_V, C.c_int, C.c_int, C.c_int, _V, _V, C.c_int, _V, _V, C.c_int,
                                       C.c_int, C.c_int, C.c_int, _V, _V, _V]),
+    "illumina_selftest": (_S, [C.c_int, _V]),
     "illumina_op_conv": (_S, [_V, C.c_int, C.c_int, C.c_int, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int,
                               _V, _V]),
     "illumina_op_lateral": (_S, [_V, C.c_int, C.c_int, _V, C.c_int, _V, _V, C.c_int, C.c_int, _V, _V]),

@@ -148,3 +148,18 @@ def test_op_argument_errors(torch):
         ops.pointwise(x, 2, 2, 6, x, x, 4, "linear")
     with pytest.raises(illumina.IlluminaError, match="kernel size must be 3 or 5"):
         ops.dwpw(x, 2, 2, 4, x, x, "linear", x, x, 4, 7, 1, "linear")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("which,name", [(0, "div6 vs IEEE a / 6.0f"), (1, "tf32_round vs cvt.rna.tf32.f32")])
+def test_arith_helpers_exhaustive(which, name):
+    """The tensor-core kernels replace two compiler operations by short
+    integer/FMA sequences (hardswish's division by 6, the TF32 rounding of the
+    3xTF32 split); both must equal the replaced operation bit for bit on every
+    non-NaN binary32 input."""
+    import ctypes as C
+    from illumina import _lib
+    out = (C.c_ulonglong * 3)()
+    _lib.check(_lib.lib().illumina_selftest(which, out))
+    assert out[0] == (1 << 32) - 2 * ((1 << 23) - 1), name   # every pattern but the NaNs
+    assert out[1] == 0, f"{name}: {out[1]} mismatches, e.g. input bits {out[2]:#010x}"
