@@ -1,8 +1,8 @@
 // Exhaustive device self-checks of the arithmetic helpers that stand in for
-// compiler-provided operations in the tensor-core kernels (tc_common.cuh):
-//   0: tcx::div6(a) against the IEEE quotient a / 6.0f,
-//   1: tcx::tf32_round(a) against cvt.rna.tf32.f32,
-// each over all 2^32 binary32 bit patterns except NaNs.
+// compiler-provided operations in the tensor-core kernels (tc_common.cuh),
+// over all 2^32 binary32 bit patterns except NaNs:
+//   0: tcx::tf32_round(a) against cvt.rna.tf32.f32,
+//   1: tcx::div6(a) against the IEEE quotient a / 6.0f.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -21,15 +21,9 @@ __global__ void k_selftest(int which, unsigned long long *out) {
     const float a = __uint_as_float(bits);
     if (isnan(a)) continue;
     checked++;
-    uint32_t got, want;
-    if (which == 0) {
-      got = __float_as_uint(illumina::gpu::tcx::div6(a));
-      want = __float_as_uint(a / 6.0f);
-    } else {
-      got = illumina::gpu::tcx::tf32_round(a);
-      want = illumina::gpu::tcx::tf32_rna(a);
-    }
-    if (got != want) {
+    const bool same = which == 0 ? illumina::gpu::tcx::tf32_round(a) == illumina::gpu::tcx::tf32_rna(a)
+                                 : __float_as_uint(illumina::gpu::tcx::div6(a)) == __float_as_uint(a / 6.0f);
+    if (!same) {
       bad++;
       atomicCAS(&out[2], 0xffffffffffffffffull, (unsigned long long)bits);
     }

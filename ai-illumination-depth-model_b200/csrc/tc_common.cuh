@@ -150,22 +150,17 @@ __device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
   hi = tf32_round(x);
   lo = tf32_round(x - __uint_as_float(hi));
 }
-// a / 6 rounded to nearest, by the quotient-by-a-known-divisor method of
-// Brisebarre, Muller and Raina ("Accelerating correctly rounded
-// floating-point division when the divisor is known in advance", IEEE Trans.
-// Computers 53(8), 2004): q = RN(a * RN(1/6)), r = a - q * 6 (exact, one FMA),
-// q' = RN(q + r * RN(1/6)). The method assumes normal intermediates, so
-// inputs below 2^-100 (quotients near the subnormal range) take the IEEE
-// division, and infinities pass through unchanged. illumina_selftest compares
-// the result bit for bit with a / 6.0f over every non-NaN binary32 input.
-__device__ __forceinline__ float div6(float a) {
-  if (fabsf(a) < 7.8886091e-31f) return a / 6.0f;  // 2^-100
-  const float c = 0.16666667f;
-  const float q = a * c;
-  const float r = fmaf(-q, 6.0f, a);
-  const float q1 = fmaf(r, c, q);
-  return isinf(q) ? q : q1;
-}
+// a / 6 rounded to nearest binary32 without the branches of the IEEE divide
+// sequence (which serialise the many independent divisions of an epilogue
+// block). The product a * RN64(1/6) in binary64 is within 2^-53 relative of
+// the exact quotient, and the quotient can never lie that close to a binary32
+// rounding midpoint: a/6 is either exactly representable (a = 6 * m) or has
+// the periodic binary expansion of a third, whose digits beyond any binary32
+// precision (normal or subnormal) are 0101... or 1010..., at least 1/6 ulp
+// away from the midpoint pattern 1000.... So rounding the binary64 product to
+// binary32 gives RN(a / 6). illumina_selftest checks it bit for bit against
+// a / 6.0f over every non-NaN binary32 input.
+__device__ __forceinline__ float div6(float a) { return __double2float_rn((double)a * (1.0 / 6.0)); }
 __device__ __forceinline__ float hardswish(float v) { return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)); }
 __device__ __forceinline__ float act_apply(int act, float v) {
   switch (act) {
@@ -219,124 +214,160 @@ struct EpiArgs {
   int n_tile;
 };
 
+// Accumulator-independent inputs of one 16-column block for the 4 rows a
+// lane stores: per row, the residual (MODE 0) or the bilinear 2x upsample of
+// the coarse map plus the residual (MODE 2).
+struct EpiBlockIn {
+  float4 x[4];
+};
+
+// Per-row pixel data of the rows a lane stores (fixed for a tile).
+struct EpiRows {
+  long m[4];  // output pixel, -1 for a padding row
+};
+
+template <typename T, int MODE>
+__device__ __forceinline__ EpiBlockIn epi_block_in(const EpiArgs &a, const EpiRows &rows, int n, bool col_ok) {
+  EpiBlockIn in;
+  const float4 z = make_float4(0, 0, 0, 0);
+  const T *res = reinterpret_cast<const T *>(a.res);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const long mm = rows.m[i];
+    in.x[i] = (col_ok && mm >= 0 && res) ? ld4(res + mm * a.N + n) : z;
+  }
+  if (MODE == 2) {
+    const T *coarse = reinterpret_cast<const T *>(a.coarse);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const long mm = rows.m[i];
+      if (!col_ok || mm < 0) continue;
+      // refUpsample2 taps (reference.ts:161-193): (i + 0.5) / 2 - 0.5, both
+      // taps from the unclamped floor, clamped independently
+      const int x = (int)(mm % a.OW);
+      const long t = mm / a.OW;
+      const int y = (int)(t % a.OH), b = (int)(t / a.OH);
+      const int CH = a.OH >> 1, CW = a.OW >> 1;
+      const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
+      const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
+      const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
+      const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
+      const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
+      const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
+      const float4 c00 = ld4(coarse + (rr0 + x0) * a.N + n), c01 = ld4(coarse + (rr0 + x1) * a.N + n);
+      const float4 c10 = ld4(coarse + (rr1 + x0) * a.N + n), c11 = ld4(coarse + (rr1 + x1) * a.N + n);
+      // the coarse term is added before the residual, as in the reference
+      float4 c;
+      c.x = c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
+      c.y = c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
+      c.z = c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
+      c.w = c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
+      in.x[i] = make_float4(c.x, c.y, c.z, c.w);  // residual of a lateral is folded in below
+      if (res) {
+        const float4 q = ld4(res + mm * a.N + n);
+        in.x[i] = make_float4(c.x + q.x, c.y + q.y, c.z + q.z, c.w + q.w);
+      }
+    }
+  }
+  return in;
+}
+
+// Issues the tcgen05.ld of one block (8 or 16 columns) into v.
+__device__ __forceinline__ void epi_block_ld(uint32_t taddr, int width, uint32_t (&v)[kEpiCols]) {
+  tmem_ld8_nowait(taddr, v);
+  if (width > 8) tmem_ld8_nowait(taddr + 8, v + 8);
+}
+
+// Moves one block's accumulator values (already waited for) into this warp's
+// shared transpose block.
+__device__ __forceinline__ void epi_block_stage(int width, const uint32_t (&v)[kEpiCols], float *blk) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kEpiCols / 4; j++)
+    if (j * 4 < width)
+      *reinterpret_cast<float4 *>(blk + lane * kEpiStride + j * 4) =
+          make_float4(__uint_as_float(v[j * 4]), __uint_as_float(v[j * 4 + 1]), __uint_as_float(v[j * 4 + 2]),
+                      __uint_as_float(v[j * 4 + 3]));
+  __syncwarp();
+}
+
+// Stores the staged block: row i*8 + lane/4, columns chunk lane%4.
+template <typename T, int ACT>
+__device__ __forceinline__ void epi_block_store(const EpiArgs &a, const EpiRows &rows, int n, bool col_ok,
+                                                const EpiBlockIn &in, const float *blk) {
+  const int lane = threadIdx.x & 31, chunk = lane & 3, rsub = lane >> 2;
+  T *dst = reinterpret_cast<T *>(a.dst);
+  if (col_ok) {
+    const float4 bias = __ldg(reinterpret_cast<const float4 *>(a.bias + n));
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (rows.m[i] < 0) continue;
+      float4 o = *reinterpret_cast<const float4 *>(blk + (i * 8 + rsub) * kEpiStride + chunk * 4);
+      o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
+      o.x += in.x[i].x, o.y += in.x[i].y, o.z += in.x[i].z, o.w += in.x[i].w;
+      st4(dst + rows.m[i] * a.N + n, act_c4<ACT>(o));
+    }
+  }
+  __syncwarp();
+}
+
 // Writes accumulator columns [col0, col0 + ncols) of the 32 TMEM lanes this
 // warp owns. Lane l handles rows i*8 + l/4 (i < 4) of the warp's 32 and
-// column chunk l%4 of every 16-column block; m[i] is that row's output pixel
-// (-1 for a padding row). Each block is read with back-to-back tcgen05.ld,
-// transposed through this warp's shared block so that every store
+// column chunk l%4 of every 16-column block. Each block is read with
+// tcgen05.ld, transposed through this warp's shared block so that every store
 // instruction writes eight 64-byte row segments (whole sectors), then
-// biased, residual/coarse-added, activated and stored. The residual of the
-// next block is loaded while the current one is processed. The tcgen05.ld
-// issue count depends only on warp-uniform values.
-template <typename T, int MODE, int ACT>
-__device__ __forceinline__ void epilogue_body(const EpiArgs &a, uint32_t tacc_lane, int col0, int ncols, int n_base,
-                                              float *blk, const long (&m)[4]) {
-  const int lane = threadIdx.x & 31, chunk = lane & 3, rsub = lane >> 2;
-  const T *res = reinterpret_cast<const T *>(a.res);
-  const T *coarse = reinterpret_cast<const T *>(a.coarse);
-  T *dst = reinterpret_cast<T *>(a.dst);
-  const long m0 = m[0], m1 = m[1], m2 = m[2], m3 = m[3];
-  const float4 z = make_float4(0, 0, 0, 0);
-  float4 r0 = z, r1 = z, r2 = z, r3 = z;  // residual of the current block
-  if (MODE != 2 && res && chunk * 4 < ncols) {
+// biased, residual/coarse-added, activated and stored.
+// Latency: everything that does not depend on the accumulator (residual,
+// coarse taps) of the first block is loaded before `ready()` waits
+// for the accumulator; once a block is staged in shared memory the next
+// block's tcgen05.ld is issued so that it is in flight while the staged block
+// is stored, and the next block's residual loads follow those stores (a
+// second block of residuals in registers would spill). Returns false when
+// `ready()` gave up. The tcgen05.ld issue count depends only on warp-uniform
+// values.
+template <typename T, int MODE, int ACT, typename ReadyFn>
+__device__ __forceinline__ bool epilogue_body(const EpiArgs &a, uint32_t tacc_lane, int col0, int ncols, int n_base,
+                                              float *blk, const EpiRows &rows, ReadyFn ready) {
+  const int chunk = (threadIdx.x & 31) & 3;
+  EpiBlockIn cur;
+  {
     const int n = n_base + col0 + chunk * 4;
-    if (n < a.N) {
-      if (m0 >= 0) r0 = ld4(res + m0 * a.N + n);
-      if (m1 >= 0) r1 = ld4(res + m1 * a.N + n);
-      if (m2 >= 0) r2 = ld4(res + m2 * a.N + n);
-      if (m3 >= 0) r3 = ld4(res + m3 * a.N + n);
-    }
+    cur = epi_block_in<T, MODE>(a, rows, n, chunk * 4 < min(kEpiCols, ncols) && n < a.N);
   }
+  if (!ready()) return false;
+  uint32_t v[kEpiCols];
+  epi_block_ld(tacc_lane + (uint32_t)col0, min(kEpiCols, ncols), v);
   for (int cb = 0; cb < ncols; cb += kEpiCols) {
-    const int width = min(kEpiCols, ncols - cb);  // 8 or 16, warp-uniform
-    uint32_t v[kEpiCols];
-    tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb), v);
-    if (width > 8) tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb + 8), v + 8);
-    // residual of the next block, in flight while this one is processed
-    float4 q0 = z, q1 = z, q2 = z, q3 = z;
-    if (MODE != 2 && res && chunk * 4 < ncols - cb - kEpiCols) {
-      const int n = n_base + col0 + cb + kEpiCols + chunk * 4;
-      if (n < a.N) {
-        if (m0 >= 0) q0 = ld4(res + m0 * a.N + n);
-        if (m1 >= 0) q1 = ld4(res + m1 * a.N + n);
-        if (m2 >= 0) q2 = ld4(res + m2 * a.N + n);
-        if (m3 >= 0) q3 = ld4(res + m3 * a.N + n);
-      }
-    }
-    tmem_wait_ld();
-#pragma unroll
-    for (int j = 0; j < kEpiCols / 4; j++)
-      if (j * 4 < width)
-        *reinterpret_cast<float4 *>(blk + lane * kEpiStride + j * 4) =
-            make_float4(__uint_as_float(v[j * 4]), __uint_as_float(v[j * 4 + 1]), __uint_as_float(v[j * 4 + 2]),
-                        __uint_as_float(v[j * 4 + 3]));
-    __syncwarp();
+    const int width = min(kEpiCols, ncols - cb);
     const int n = n_base + col0 + cb + chunk * 4;
     const bool col_ok = chunk * 4 < width && n < a.N;
-    float4 bias = z;
-    if (col_ok) bias = __ldg(reinterpret_cast<const float4 *>(a.bias + n));
-    if (MODE == 2) {
-#pragma unroll 1
-      for (int i = 0; i < 4; i++) {
-        const long mm = m[i];
-        if (!col_ok || mm < 0) continue;
-        float4 o = *reinterpret_cast<const float4 *>(blk + (i * 8 + rsub) * kEpiStride + chunk * 4);
-        o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
-        // refUpsample2 taps (reference.ts:161-193): (i + 0.5) / 2 - 0.5, both
-        // taps from the unclamped floor, clamped independently
-        const int x = (int)(mm % a.OW);
-        const long t = mm / a.OW;
-        const int y = (int)(t % a.OH), b = (int)(t / a.OH);
-        const int CH = a.OH >> 1, CW = a.OW >> 1;
-        const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
-        const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
-        const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
-        const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
-        const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
-        const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
-        const float4 c00 = ld4(coarse + (rr0 + x0) * a.N + n), c01 = ld4(coarse + (rr0 + x1) * a.N + n);
-        const float4 c10 = ld4(coarse + (rr1 + x0) * a.N + n), c11 = ld4(coarse + (rr1 + x1) * a.N + n);
-        o.x += c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
-        o.y += c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
-        o.z += c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
-        o.w += c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
-        if (res) {
-          const float4 q = ld4(res + mm * a.N + n);
-          o.x += q.x, o.y += q.y, o.z += q.z, o.w += q.w;
-        }
-        st4(dst + mm * a.N + n, act_c4<ACT>(o));
-      }
-    } else if (col_ok) {
-      const float4 rr[4] = {r0, r1, r2, r3};
-      const long mr[4] = {m0, m1, m2, m3};
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        if (mr[i] < 0) continue;
-        float4 o = *reinterpret_cast<const float4 *>(blk + (i * 8 + rsub) * kEpiStride + chunk * 4);
-        o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
-        o.x += rr[i].x, o.y += rr[i].y, o.z += rr[i].z, o.w += rr[i].w;
-        st4(dst + mr[i] * a.N + n, act_c4<ACT>(o));
-      }
-    }
-    __syncwarp();
-    r0 = q0, r1 = q1, r2 = q2, r3 = q3;
+    const int cb1 = cb + kEpiCols;
+    const int n1 = n + kEpiCols;
+    const bool ok1 = cb1 < ncols && chunk * 4 < min(kEpiCols, ncols - cb1) && n1 < a.N;
+    tmem_wait_ld();
+    epi_block_stage(width, v, blk);
+    if (cb1 < ncols) epi_block_ld(tacc_lane + (uint32_t)(col0 + cb1), min(kEpiCols, ncols - cb1), v);
+    epi_block_store<T, ACT>(a, rows, n, col_ok, cur, blk);
+    if (cb1 < ncols) cur = epi_block_in<T, MODE>(a, rows, n1, ok1);
   }
+  return true;
 }
 
 // `pix(r)` maps a tile row (0..127) to its output pixel, or -1 for a padding
-// row; `lane_base` is the first of the warp's 32 TMEM lanes.
-template <typename T, int MODE, typename PixFn>
-__device__ __forceinline__ void epilogue_rows(const EpiArgs &a, uint32_t tacc_lane, int lane_base, int col0, int ncols,
-                                              int n_base, float *blk, PixFn pix) {
+// row; `lane_base` is the first of the warp's 32 TMEM lanes; `ready()` waits
+// (bounded) for the accumulator and returns false when it gave up.
+template <typename T, int MODE, typename PixFn, typename ReadyFn>
+__device__ __forceinline__ bool epilogue_rows(const EpiArgs &a, uint32_t tacc_lane, int lane_base, int col0, int ncols,
+                                              int n_base, float *blk, PixFn pix, ReadyFn ready) {
   const int rsub = (threadIdx.x & 31) >> 2;
-  long m[4];
+  EpiRows rows;
 #pragma unroll
-  for (int i = 0; i < 4; i++) m[i] = pix(lane_base + i * 8 + rsub);
+  for (int i = 0; i < 4; i++) rows.m[i] = pix(lane_base + i * 8 + rsub);
   switch (a.act) {
-    case 1: epilogue_body<T, MODE, 1>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
-    case 2: epilogue_body<T, MODE, 2>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
-    case 3: epilogue_body<T, MODE, 3>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
-    default: epilogue_body<T, MODE, 0>(a, tacc_lane, col0, ncols, n_base, blk, m); break;
+    case 1: return epilogue_body<T, MODE, 1>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
+    case 2: return epilogue_body<T, MODE, 2>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
+    case 3: return epilogue_body<T, MODE, 3>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
+    default: return epilogue_body<T, MODE, 0>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
   }
 }
 

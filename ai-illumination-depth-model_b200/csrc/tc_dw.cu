@@ -28,7 +28,8 @@
 //   warp 1        one thread issues tcgen05.mma into one of two TMEM
 //                 accumulators and commits each G stage back to the ring.
 //   warps 10-13   epilogue (tcx::epilogue_rows), one warp per TMEM lane
-//                 quarter: bias, residual, activation, store; then release
+//                 quarter: bias and residual loaded before the accumulator
+//                 is waited for, then activation and store; then release
 //                 the accumulator.
 // A ring stage is always used by the same depthwise group (the ring depths
 // are multiples of ng), so a group's own previous use of a stage orders its
@@ -351,18 +352,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     const int tw = p.tw, th = p.th, OH = p.epi.OH, OW = p.epi.OW;
     for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
       const Item it = decode(p, t);
-      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase))) {
+      uint64_t *full = &acc_full[acc];
+      const uint32_t ph = acc_phase;
+      if (!epilogue_rows<T, 0>(
+              p.epi, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base, 0, n_tile,
+              it.nt * n_tile, blk,
+              [=](int r) -> long {
+                const int ly = r / tw, lx = r - ly * tw;
+                const int y = it.y0 + ly, x = it.x0 + lx;
+                if (ly >= th || y >= OH || x >= OW) return -1;
+                return ((long)it.b * OH + y) * OW + x;
+              },
+              [full, ph]() {
+                const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph));
+                tc_fence_after();
+                return w;
+              })) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      epilogue_rows<T, 0>(p.epi, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base, 0,
-                          n_tile, it.nt * n_tile, blk, [=](int r) -> long {
-                            const int ly = r / tw, lx = r - ly * tw;
-                            const int y = it.y0 + ly, x = it.x0 + lx;
-                            if (ly >= th || y >= OH || x >= OW) return -1;
-                            return ((long)it.b * OH + y) * OW + x;
-                          });
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);

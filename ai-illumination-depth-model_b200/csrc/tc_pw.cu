@@ -15,8 +15,10 @@
 //                 kind::f16 MMA for bf16), commits each stage back to `empty`
 //                 and each finished tile to `acc_full`.
 //   warps 6-13    epilogue (tcx::epilogue_rows): two warps per TMEM lane
-//                 quarter, one per column half; then release the accumulator
-//                 (`acc_empty`) so the next tile's MMAs overlap these stores.
+//                 quarter, one per column half; loads what does not depend on
+//                 the accumulator (bias, residual, coarse taps) before waiting
+//                 for it, then releases it (`acc_empty`) so the next tile's
+//                 MMAs overlap these stores.
 // Every mbarrier wait is bounded; a role that gives up records it in *err and
 // leaves its loop; all roles meet before TMEM is released.
 #include <cudaTypedefs.h>
@@ -176,16 +178,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
-      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase))) {
+      const long m0 = (long)mt * kTileM;
+      const long M = p.M;
+      uint64_t *full = &acc_full[acc];
+      const uint32_t ph = acc_phase;
+      if (!epilogue_rows<T, MODE>(p.epi, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base,
+                                  (e >> 2) * half, half, nt * n_tile, blk,
+                                  [m0, M](int r) -> long { return m0 + r < M ? m0 + r : -1; },
+                                  [full, ph]() {
+                                    const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph));
+                                    tc_fence_after();
+                                    return w;
+                                  })) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      const long m0 = (long)mt * kTileM;
-      const long M = p.M;
-      epilogue_rows<T, MODE>(p.epi, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base,
-                             (e >> 2) * half, half, nt * n_tile, blk,
-                             [m0, M](int r) -> long { return m0 + r < M ? m0 + r : -1; });
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);

@@ -355,11 +355,11 @@ illumina_status illumina_checksums(const float *maps, int n, long count, uint64_
 
 /* Exhaustive device check of an arithmetic helper of the tensor-core kernels
  * against the operation it replaces, over all 2^32 binary32 bit patterns
- * except NaNs: which = 0 the division by 6 of hardswish against the IEEE
- * quotient, which = 1 the TF32 rounding of the hi/lo split against
- * cvt.rna.tf32.f32. result (host, 3 values): inputs checked, mismatches, and
- * the bits of one mismatching input (all ones when there is none). Runs on the
- * current device, synchronously. No counterpart in the reference. */
+ * except NaNs: which = 0 the TF32 rounding of the 3xTF32 hi/lo split against
+ * cvt.rna.tf32.f32, which = 1 the division by 6 of hardswish against the IEEE
+ * quotient. result (host, 3 values): inputs checked, mismatches, and the bits
+ * of one mismatching input (all ones when there is none). Runs on the current
+ * device, synchronously. No counterpart in the reference. */
 illumina_status illumina_selftest(int which, unsigned long long *result);
 
 #ifdef __cplusplus
