@@ -83,6 +83,18 @@ __device__ __forceinline__ float srgb_to_linear(float c) {
 
 static inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads - 1) / threads); }
 
+// idx = (b * H + y) * W + x, split with 32-bit division (64-bit division is a
+// long software sequence); launches check that their index range is below 2^31.
+__device__ __forceinline__ void unflatten3(long idx, int W, int H, int &x, int &y, int &b) {
+  const uint32_t u = (uint32_t)idx, uw = (uint32_t)W, uh = (uint32_t)H;
+  const uint32_t t = u / uw;
+  x = (int)(u - t * uw);
+  const uint32_t bb = t / uh;
+  y = (int)(t - bb * uh);
+  b = (int)bb;
+}
+constexpr long kMaxIndex = 0x7fffffffL;
+
 // ---------------------------------------------------------------------------
 // preprocess (src/model/kernels/io.ts:64-118 semantics, refPreprocess)
 // ---------------------------------------------------------------------------
@@ -94,7 +106,8 @@ __global__ void k_preprocess(const float *__restrict__ frames, int layout, long 
   long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   long plane = (long)S * S;
-  long b = idx / plane, pix = idx - b * plane;
+  const uint32_t ub = (uint32_t)idx / (uint32_t)plane;
+  long b = ub, pix = idx - b * plane;
   float r, g, bl;
   if (layout == 0) {
     const float *f = frames + b * 3 * plane + pix;
@@ -115,6 +128,7 @@ __global__ void k_preprocess(const float *__restrict__ frames, int layout, long 
 cudaError_t preprocess(int T, const float *frames, int layout, int n, int S, const PreprocessParams &p, void *input,
                        float *luma, float *scene, cudaStream_t st) {
   long total = (long)n * S * S;
+  if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
   if (T == F32)
     k_preprocess<float><<<blocks_for(total, 256), 256, 0, st>>>(frames, layout, total, S, p, (float *)input, luma,
@@ -137,10 +151,8 @@ __global__ void k_conv(const T *__restrict__ src, int n, int H, int W, int Cin, 
   long total = (long)n * OH * OW;
   if (pix >= total) return;
   int og = blockIdx.y;  // group of 16 output channels
-  int ox = (int)(pix % OW);
-  long t = pix / OW;
-  int oy = (int)(t % OH);
-  int b = (int)(t / OH);
+  int ox, oy, b;
+  unflatten3(pix, OW, OH, ox, oy, b);
   int pad = (k - 1) >> 1;
   int cout4 = Cout >> 2, cin4 = Cin >> 2;
   int g0 = og * 4;
@@ -190,6 +202,7 @@ cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const flo
   int pad = (k - 1) >> 1;
   int OH = (H + 2 * pad - k) / stride + 1, OW = (W + 2 * pad - k) / stride + 1;
   long total = (long)n * OH * OW;
+  if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total <= 0) return cudaSuccess;
   dim3 grid(blocks_for(total, 128), (Cout / 4 + 3) / 4);
   if (T == F32)
@@ -484,10 +497,8 @@ __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh
   long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   long total = (long)n * S * SW;
   if (idx >= total) return;
-  int x = (int)(idx % SW);
-  long t = idx / SW;
-  int y = (int)(t % S);
-  int b = (int)(t / S);
+  int x, y, b;
+  unflatten3(idx, SW, S, x, y, b);
   auto luma_at = [&](int gx, int gy) -> float {
     long g = ((long)b * S + gy) * SW + gx;
     if (luma) return __ldg(luma + g);
@@ -528,6 +539,7 @@ __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh
 cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *luma, const BilateralParams &p,
                       float *dst, const float *history, float *out_tex, cudaStream_t st) {
   long total = (long)n * lh * lw * 4;
+  if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
   k_bilateral<<<blocks_for(total, 256), 256, 0, st>>>(low1, 1, n, lh, lw, luma, nullptr, 0, p, dst, history,
                                                       out_tex);
@@ -537,6 +549,7 @@ cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *lum
 cudaError_t bilateral_strided(const float *low, int lh, int lw, int low_c, const float *guide, int guide_c,
                               float range_sigma, float *dst, cudaStream_t st) {
   long total = (long)lh * lw * 4;
+  if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
   BilateralParams p{range_sigma, 0.35f, 3.0f};
   k_bilateral<<<blocks_for(total, 256), 256, 0, st>>>(low, low_c, 1, lh, lw, nullptr, guide, guide_c, p, dst,

@@ -152,14 +152,15 @@ __device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
 }
 // a / 6 rounded to nearest binary32 without the branches of the IEEE divide
 // sequence (which serialise the many independent divisions of an epilogue
-// block). The product a * RN64(1/6) in binary64 is within 2^-53 relative of
-// the exact quotient, and the quotient can never lie that close to a binary32
-// rounding midpoint: a/6 is either exactly representable (a = 6 * m) or has
-// the periodic binary expansion of a third, whose digits beyond any binary32
-// precision (normal or subnormal) are 0101... or 1010..., at least 1/6 ulp
-// away from the midpoint pattern 1000.... So rounding the binary64 product to
-// binary32 gives RN(a / 6). illumina_selftest checks it bit for bit against
-// a / 6.0f over every non-NaN binary32 input.
+// block or a depthwise run). The product a * RN64(1/6) in binary64 is within
+// 2^-53 relative of the exact quotient, and the quotient can never lie that
+// close to a binary32 rounding midpoint: a / 6 is either exactly
+// representable or has the periodic binary expansion of a third, whose digits
+// beyond any binary32 precision (normal or subnormal) are 0101... or 1010...,
+// at least 1/6 ulp away from the midpoint pattern 1000.... So rounding the
+// binary64 product to binary32 gives RN(a / 6). (A binary32 FMA-corrected
+// quotient with a guard for tiny inputs measured slower.) illumina_selftest
+// checks it bit for bit against a / 6.0f over every non-NaN binary32 input.
 __device__ __forceinline__ float div6(float a) { return __double2float_rn((double)a * (1.0 / 6.0)); }
 __device__ __forceinline__ float hardswish(float v) { return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)); }
 __device__ __forceinline__ float act_apply(int act, float v) {
@@ -182,6 +183,12 @@ __device__ __forceinline__ float act_c(float v) {
 template <int ACT>
 __device__ __forceinline__ float4 act_c4(float4 v) {
   return make_float4(act_c<ACT>(v.x), act_c<ACT>(v.y), act_c<ACT>(v.z), act_c<ACT>(v.w));
+}
+// ACT applied to NV float4 values in place.
+template <int ACT, int NV>
+__device__ __forceinline__ void act_n(float4 (&v)[NV]) {
+#pragma unroll
+  for (int i = 0; i < NV; i++) v[i] = act_c4<ACT>(v[i]);
 }
 __device__ __forceinline__ float4 act4(int act, float4 v) {
   return make_float4(act_apply(act, v.x), act_apply(act, v.y), act_apply(act, v.z), act_apply(act, v.w));
@@ -206,7 +213,7 @@ __device__ __forceinline__ float4 f4fma(float4 a, float4 b, float4 c) {
 }
 
 struct EpiArgs {
-  const float *bias;
+  const float *bias;   // [N]; the kernels pass a shared-memory copy
   const void *res;     // [M][N] or null
   const void *coarse;  // lateral: (n, OH/2, OW/2, N) or null
   void *dst;           // [M][N]
@@ -244,9 +251,13 @@ __device__ __forceinline__ EpiBlockIn epi_block_in(const EpiArgs &a, const EpiRo
       if (!col_ok || mm < 0) continue;
       // refUpsample2 taps (reference.ts:161-193): (i + 0.5) / 2 - 0.5, both
       // taps from the unclamped floor, clamped independently
-      const int x = (int)(mm % a.OW);
-      const long t = mm / a.OW;
-      const int y = (int)(t % a.OH), b = (int)(t / a.OH);
+      // pixel indices stay below 2^31 (frames x OH x OW of one launch), so the
+      // decomposition uses 32-bit division
+      const uint32_t um = (uint32_t)mm, uow = (uint32_t)a.OW, uoh = (uint32_t)a.OH;
+      const uint32_t t = um / uow;
+      const int x = (int)(um - t * uow);
+      const uint32_t bb = t / uoh;
+      const int y = (int)(t - bb * uoh), b = (int)bb;
       const int CH = a.OH >> 1, CW = a.OW >> 1;
       const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
       const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
@@ -291,22 +302,26 @@ __device__ __forceinline__ void epi_block_stage(int width, const uint32_t (&v)[k
   __syncwarp();
 }
 
-// Stores the staged block: row i*8 + lane/4, columns chunk lane%4.
+// Stores the staged block: row i*8 + lane/4, columns chunk lane%4. `a.bias`
+// may point to shared memory (generic load).
 template <typename T, int ACT>
 __device__ __forceinline__ void epi_block_store(const EpiArgs &a, const EpiRows &rows, int n, bool col_ok,
                                                 const EpiBlockIn &in, const float *blk) {
   const int lane = threadIdx.x & 31, chunk = lane & 3, rsub = lane >> 2;
   T *dst = reinterpret_cast<T *>(a.dst);
   if (col_ok) {
-    const float4 bias = __ldg(reinterpret_cast<const float4 *>(a.bias + n));
+    const float4 bias = *reinterpret_cast<const float4 *>(a.bias + n);
+    float4 o[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      if (rows.m[i] < 0) continue;
-      float4 o = *reinterpret_cast<const float4 *>(blk + (i * 8 + rsub) * kEpiStride + chunk * 4);
-      o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
-      o.x += in.x[i].x, o.y += in.x[i].y, o.z += in.x[i].z, o.w += in.x[i].w;
-      st4(dst + rows.m[i] * a.N + n, act_c4<ACT>(o));
+      o[i] = *reinterpret_cast<const float4 *>(blk + (i * 8 + rsub) * kEpiStride + chunk * 4);
+      o[i].x += bias.x, o[i].y += bias.y, o[i].z += bias.z, o[i].w += bias.w;
+      o[i].x += in.x[i].x, o[i].y += in.x[i].y, o[i].z += in.x[i].z, o[i].w += in.x[i].w;
     }
+    act_n<ACT, 4>(o);
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (rows.m[i] >= 0) st4(dst + rows.m[i] * a.N + n, o[i]);
   }
   __syncwarp();
 }

@@ -67,7 +67,7 @@ struct Params {
   int tiles_x, tiles_y, n_tiles, slabs, total;
   int tw, th, iw, mid_act;
   int sh, sg, b_res, ng;
-  uint32_t halo_bytes, dw_bytes, h_stage, g_stage, b_bytes, acc_stride, tmem_cols;
+  uint32_t halo_bytes, dw_bytes, h_stage, g_stage, b_bytes, acc_stride, tmem_cols, bias_bytes;
 };
 
 struct Item {
@@ -184,7 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
   uint8_t *bres = gbase + p.sg * p.g_stage;
   const uint32_t res_bytes = p.b_res ? (uint32_t)(p.n_tiles * p.slabs) * p.b_bytes : 0u;
   float *epi_smem = reinterpret_cast<float *>(bres + res_bytes);
-  uint64_t *h_full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(epi_smem) + kEpiBytes);
+  float *bias_smem = epi_smem + kEpiBytes / 4;
+  uint64_t *h_full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(bias_smem) + p.bias_bytes);
   uint64_t *h_empty = h_full + p.sh;
   uint64_t *g_full = h_empty + p.sh;
   uint64_t *a_ready = g_full + p.sg;
@@ -215,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     mbar_init(drain, 1);
     fence_barrier_init();
   }
+  for (int i = tid; i < p.epi.N; i += kThreads) bias_smem[i] = p.epi.bias[i];
   if (warp == 0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
   __syncthreads();
@@ -350,12 +352,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     int acc = 0;
     uint32_t acc_phase = 0;
     const int tw = p.tw, th = p.th, OH = p.epi.OH, OW = p.epi.OW;
+    EpiArgs ea = p.epi;
+    ea.bias = bias_smem;
     for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
       const Item it = decode(p, t);
       uint64_t *full = &acc_full[acc];
       const uint32_t ph = acc_phase;
       if (!epilogue_rows<T, 0>(
-              p.epi, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base, 0, n_tile,
+              ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base, 0, n_tile,
               it.nt * n_tile, blk,
               [=](int r) -> long {
                 const int ly = r / tw, lx = r - ly * tw;
@@ -425,6 +429,7 @@ struct DwTiling {
 // groups interleave; the MMAs (fp32: 16 TF32 MMAs) and the halo bandwidth
 // bound the step from below. The epilogue of an item overlaps the next item.
 DwTiling plan_tiling(int T, int OH, int OW, int KS, int S, const TcWeights &w, bool has_res) {
+  const size_t bias_bytes = align_to((size_t)w.N * 4, 16);
   const bool f32 = T == F32;
   const int terms = f32 ? 2 : 1, slab_c = f32 ? 32 : 64, cgs = slab_c / 4;
   const size_t dw_bytes = (size_t)(KS * KS + 1) * slab_c * 4;
@@ -456,7 +461,7 @@ DwTiling plan_tiling(int T, int OH, int OW, int KS, int S, const TcWeights &w, b
           for (int sh = ng; sh <= 4; sh += ng) {
             for (int sg = ng; sg <= 4; sg += ng) {
               const size_t smem = 1024 + sh * h_stage + sg * g_stage + (b_res ? res_total : 0) + tcd::kEpiBytes +
-                                  8 * (2 * sh + 3 * sg + 6) + 16;
+                                  bias_bytes + 8 * (2 * sh + 3 * sg + 6) + 16;
               if (smem > kSmemBudget) continue;
               double group = sh / ng >= 2 ? std::fmax(lat, xf) : lat + xf;
               if (sg / ng < 2) group += mma;
@@ -578,6 +583,7 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.acc_stride = 32;
   while ((int)p.acc_stride < plan.n_tile) p.acc_stride <<= 1;
   p.tmem_cols = 2 * p.acc_stride;
+  p.bias_bytes = (uint32_t)align_to((size_t)op.N * 4, 16);
   if (T == F32) return launch_t<float>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
   return launch_t<__nv_bfloat16>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
 }

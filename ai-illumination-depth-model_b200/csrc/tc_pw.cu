@@ -43,7 +43,7 @@ struct Params {
   int *err;
   long M;
   int n_tiles, m_tiles, slabs, stages;
-  uint32_t acc_stride, tmem_cols, b_bytes;
+  uint32_t acc_stride, tmem_cols, b_bytes, bias_bytes;
 };
 
 // MODE 0 pointwise, 2 lateral.
@@ -59,7 +59,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
   const uint32_t stage_bytes = kTerms * kAImage + p.b_bytes;
   const int S = p.stages;
   float *epi_smem = reinterpret_cast<float *>(base + S * stage_bytes);
-  uint64_t *full = reinterpret_cast<uint64_t *>(base + S * stage_bytes + kEpiSmem);
+  float *bias_smem = epi_smem + kEpiSmem / 4;
+  uint64_t *full = reinterpret_cast<uint64_t *>(base + S * stage_bytes + kEpiSmem + p.bias_bytes);
   uint64_t *lo_rdy = full + S;
   uint64_t *empty = lo_rdy + S;
   uint64_t *acc_full = empty + S;
@@ -80,6 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     }
     fence_barrier_init();
   }
+  for (int i = tid; i < p.epi.N; i += kThreads) bias_smem[i] = p.epi.bias[i];
   if (warp == 0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
   __syncthreads();
@@ -176,13 +178,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     float *blk = epi_smem + e * 32 * kEpiStride;
     int acc = 0;
     uint32_t acc_phase = 0;
+    EpiArgs ea = p.epi;
+    ea.bias = bias_smem;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
       const long m0 = (long)mt * kTileM;
       const long M = p.M;
       uint64_t *full = &acc_full[acc];
       const uint32_t ph = acc_phase;
-      if (!epilogue_rows<T, MODE>(p.epi, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base,
+      if (!epilogue_rows<T, MODE>(ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base,
                                   (e >> 2) * half, half, nt * n_tile, blk,
                                   [m0, M](int r) -> long { return m0 + r < M ? m0 + r : -1; },
                                   [full, ph]() {
@@ -264,6 +268,7 @@ cudaError_t launch(const CUtensorMap &map, const tcp::Params &p, size_t smem, cu
 cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st) {
   if (op.M <= 0) return cudaSuccess;
   if (op.mode != 0 && op.mode != 2) return cudaErrorInvalidValue;
+  if (op.M > 0x7fffffffL) return cudaErrorInvalidValue;  // the epilogue decomposes pixels in 32 bits
   auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
   const size_t elt = T == F32 ? 4 : 2;
@@ -290,12 +295,13 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.tmem_cols = 2 * p.acc_stride;
   p.b_bytes = (uint32_t)(terms * plan.n_tile * 128);
   const size_t stage = terms * tcx::kAImage + p.b_bytes;
-  const size_t fixed = 1024 + tcx::kEpiSmem + 8 * (3 * 8 + 4) + 16;
+  p.bias_bytes = (uint32_t)(((size_t)op.N * 4 + 15) / 16 * 16);
+  const size_t fixed = 1024 + tcx::kEpiSmem + p.bias_bytes + 8 * (3 * 8 + 4) + 16;
   int stages = (int)((kSmemBudget - fixed) / stage);
   if (stages > 6) stages = 6;
   if (stages < 2) return cudaErrorInvalidValue;
   p.stages = stages;
-  const size_t smem = stages * stage + 1024 + tcx::kEpiSmem + 8 * (3 * stages + 4) + 16;
+  const size_t smem = stages * stage + 1024 + tcx::kEpiSmem + p.bias_bytes + 8 * (3 * stages + 4) + 16;
   if (T == F32) return op.mode == 0 ? launch<float, 0>(map, p, smem, st) : launch<float, 2>(map, p, smem, st);
   return op.mode == 0 ? launch<__nv_bfloat16, 0>(map, p, smem, st) : launch<__nv_bfloat16, 2>(map, p, smem, st);
 }
