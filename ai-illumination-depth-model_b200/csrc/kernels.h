@@ -49,6 +49,13 @@ struct GemmOp {
   const float *dw_w = nullptr;   // packed [ks*ks][K]
   const float *dw_b = nullptr;   // [K]
   const void *coarse = nullptr;  // lateral: (n, H/2, W/2, N)
+  // Optional split-K workspace of the tensor-core dw->pw kernel: fp32 partial
+  // tiles and one zero-initialised arrival counter per work item (the kernel
+  // leaves them zero again). Without it the kernel does not split K.
+  float *ws = nullptr;
+  size_t ws_bytes = 0;
+  int *ws_cnt = nullptr;
+  int ws_cnt_n = 0;
 };
 
 cudaError_t gemm(int T, const GemmOp &op, cudaStream_t st);

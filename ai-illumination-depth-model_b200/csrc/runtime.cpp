@@ -49,6 +49,14 @@ void set_last_error(const std::string &msg) { g_last_error = msg; }
 
 namespace {
 
+// Split-K workspace of the tensor-core dw->pw kernel: a model holds 16 MiB of
+// fp32 partial tiles and 8192 arrival counters (the planner splits K only
+// when a launch's partials fit); a per-kernel entry point call takes 8 MiB.
+constexpr size_t kSplitKBytes = 16u << 20;
+constexpr int kSplitKItems = 8192;
+constexpr size_t kSplitKOpBytes = 8u << 20;
+constexpr int kSplitKOpItems = 4096;
+
 void cuda_check(cudaError_t e, const char *what) {
   if (e != cudaSuccess)
     throw Error(ILLUMINA_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
@@ -128,6 +136,8 @@ struct illumina_model {
   std::vector<size_t> tc_off;        // per op: byte offset into d_wimg
   uint8_t *d_wimg = nullptr;         // tensor-core weight images
   int *d_err = nullptr;              // set by a kernel that gave up a bounded wait
+  float *d_splitk = nullptr;         // split-K partial tiles of the tensor dw->pw kernel
+  int *d_splitk_cnt = nullptr;       // its per-item arrival counters (zero between launches)
 
   void *tensor(const std::string &name) {
     auto it = plan.assignment.find(name);
@@ -159,6 +169,8 @@ illumina_model::~illumina_model() {
   cudaFree(d_stage_low);
   cudaFree(d_wimg);
   cudaFree(d_err);
+  cudaFree(d_splitk);
+  cudaFree(d_splitk_cnt);
   if (ev_join) cudaEventDestroy(ev_join);
   if (ev_done) cudaEventDestroy(ev_done);
   if (stream) cudaStreamDestroy(stream);
@@ -259,6 +271,8 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
             g.ks = op.k, g.stride = op.stride;
             g.mid_act = op.mid_act;
             g.dw_w = w.dw_w, g.dw_b = w.dw_b;
+            g.ws = m.d_splitk, g.ws_bytes = m.d_splitk ? kSplitKBytes : 0;
+            g.ws_cnt = m.d_splitk_cnt, g.ws_cnt_n = m.d_splitk_cnt ? kSplitKItems : 0;
           } else {
             g.mode = 0;
           }
@@ -528,6 +542,12 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
   m.engine = o.gemm_engine;
   cuda_check(cudaMalloc(&m.d_err, sizeof(int)), "cudaMalloc error flag");
   cuda_check(cudaMemsetAsync(m.d_err, 0, sizeof(int), m.stream), "clear error flag");
+  if (o.gemm_engine == ILLUMINA_ENGINE_TENSOR) {
+    cuda_check(cudaMalloc(&m.d_splitk, kSplitKBytes), "cudaMalloc split-K workspace");
+    cuda_check(cudaMalloc(&m.d_splitk_cnt, kSplitKItems * sizeof(int)), "cudaMalloc split-K counters");
+    cuda_check(cudaMemsetAsync(m.d_splitk_cnt, 0, kSplitKItems * sizeof(int), m.stream), "clear split-K counters");
+    m.device_bytes += kSplitKBytes + kSplitKItems * sizeof(int);
+  }
   m.tcw.resize(m.arch.ops.size());
   m.tc_off.assign(m.arch.ops.size(), 0);
   if (m.engine == ILLUMINA_ENGINE_TENSOR) {
@@ -614,9 +634,16 @@ void op_gemm(const gpu::GemmOp &g, cudaStream_t st, const char *what) {
   Scratch img(plan.bytes, st);
   cuda_check(cudaMemsetAsync(img.p, 0, plan.bytes, st), "clear weight images");
   cuda_check(gpu::tc_pack(gpu::F32, g.w, g.N, g.K, plan, (uint8_t *)img.p, st), "pack weight images");
-  if (g.mode == 1)
-    cuda_check(gpu::tc_pack_dw(gpu::F32, g.dw_w, g.dw_b, plan, (uint8_t *)img.p, st), "pack depthwise blocks");
-  cuda_check(gpu::tc_op(gpu::F32, g, plan, (const uint8_t *)img.p, nullptr, st), what);
+  if (g.mode != 1) {
+    cuda_check(gpu::tc_op(gpu::F32, g, plan, (const uint8_t *)img.p, nullptr, st), what);
+    return;
+  }
+  cuda_check(gpu::tc_pack_dw(gpu::F32, g.dw_w, g.dw_b, plan, (uint8_t *)img.p, st), "pack depthwise blocks");
+  Scratch ws(kSplitKOpBytes, st), cnt(kSplitKOpItems * sizeof(int), st);
+  cuda_check(cudaMemsetAsync(cnt.p, 0, kSplitKOpItems * sizeof(int), st), "clear split-K counters");
+  gpu::GemmOp gs = g;
+  gs.ws = (float *)ws.p, gs.ws_bytes = kSplitKOpBytes, gs.ws_cnt = (int *)cnt.p, gs.ws_cnt_n = kSplitKOpItems;
+  cuda_check(gpu::tc_op(gpu::F32, gs, plan, (const uint8_t *)img.p, nullptr, st), what);
 }
 
 }  // namespace

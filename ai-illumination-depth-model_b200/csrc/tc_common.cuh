@@ -368,6 +368,93 @@ __device__ __forceinline__ bool epilogue_body(const EpiArgs &a, uint32_t tacc_la
   return true;
 }
 
+// Split-K: writes the fp32 accumulator columns [0, ncols) of this warp's 32
+// TMEM lanes as rows lane_base + lane of a [128][ld] partial tile (no bias,
+// no activation). Bypasses L1: another SM reads the tile.
+__device__ __forceinline__ void store_partial(uint32_t tacc_lane, int lane_base, int ncols, float *tile, int ld) {
+  const int lane = threadIdx.x & 31;
+  float *row = tile + (size_t)(lane_base + lane) * ld;
+  for (int cb = 0; cb < ncols; cb += kEpiCols) {
+    const int width = min(kEpiCols, ncols - cb);
+    uint32_t v[kEpiCols];
+    epi_block_ld(tacc_lane + (uint32_t)cb, width, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < kEpiCols / 4; j++)
+      if (j * 4 < width)
+        __stcg(reinterpret_cast<float4 *>(row + cb + j * 4),
+               make_float4(__uint_as_float(v[j * 4]), __uint_as_float(v[j * 4 + 1]), __uint_as_float(v[j * 4 + 2]),
+                           __uint_as_float(v[j * 4 + 3])));
+  }
+}
+
+// Split-K: sums the ksplit partial tiles of one item ([ksplit][128][ld] at
+// `part`, split order fixed so the result does not depend on which CTA
+// finished last), then bias, residual, activation and store, for this warp's
+// rows and columns [0, ncols) (output columns n_base + c). Same lane layout as
+// epilogue_body; partials are read past L1 (written by other SMs).
+template <typename T, int ACT>
+__device__ __forceinline__ void reduce_body(const EpiArgs &a, const float *part, int ksplit, size_t split_stride,
+                                            int ld, int lane_base, int ncols, int n_base, const EpiRows &rows) {
+  const int lane = threadIdx.x & 31, chunk = lane & 3, rsub = lane >> 2;
+  const T *res = reinterpret_cast<const T *>(a.res);
+  T *dst = reinterpret_cast<T *>(a.dst);
+  for (int cb = 0; cb < ncols; cb += kEpiCols) {
+    const int c = cb + chunk * 4;
+    const int n = n_base + c;
+    if (chunk * 4 >= min(kEpiCols, ncols - cb) || n >= a.N) continue;
+    float4 o[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) o[i] = make_float4(0, 0, 0, 0);
+    for (int j = 0; j < ksplit; j++) {
+      const float *pj = part + j * split_stride + c;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 q = __ldcg(reinterpret_cast<const float4 *>(pj + (size_t)(lane_base + i * 8 + rsub) * ld));
+        o[i].x += q.x, o[i].y += q.y, o[i].z += q.z, o[i].w += q.w;
+      }
+    }
+    const float4 bias = *reinterpret_cast<const float4 *>(a.bias + n);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      o[i].x += bias.x, o[i].y += bias.y, o[i].z += bias.z, o[i].w += bias.w;
+      if (res && rows.m[i] >= 0) {
+        const float4 q = ld4(res + rows.m[i] * a.N + n);
+        o[i].x += q.x, o[i].y += q.y, o[i].z += q.z, o[i].w += q.w;
+      }
+    }
+    act_n<ACT, 4>(o);
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (rows.m[i] >= 0) st4(dst + rows.m[i] * a.N + n, o[i]);
+  }
+}
+
+// Out of line: the reduction's registers stay out of the persistent loop that
+// calls it (inlined, they made the common unsplit path spill).
+template <typename T>
+__device__ __noinline__ void epilogue_reduce(const EpiArgs a, const float *part, int ksplit, size_t split_stride, int ld,
+                                             int lane_base, int ncols, int n_base, const EpiRows rows) {
+  switch (a.act) {
+    case 1: reduce_body<T, 1>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
+    case 2: reduce_body<T, 2>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
+    case 3: reduce_body<T, 3>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
+    default: reduce_body<T, 0>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
+  }
+}
+
+// Named barrier `id` over `n` threads; returns the AND of `v` over them.
+__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_named(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
 // `pix(r)` maps a tile row (0..127) to its output pixel, or -1 for a padding
 // row; `lane_base` is the first of the warp's 32 TMEM lanes; `ready()` waits
 // (bounded) for the accumulator and returns false when it gave up.

@@ -39,355 +39,21 @@
 // is released.
 #include <cudaTypedefs.h>
 
+#include <array>
 #include <cmath>
+#include <map>
+#include <mutex>
 
 #include "kernels.h"
 #include "tc_common.cuh"
+#include "tc_dw_kernel.cuh"
 
 namespace illumina {
 namespace gpu {
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
-int sm_count();
 
 namespace tcd {
-
-using namespace tcx;
-
-constexpr int kMmaWarp = 1, kXfWarp0 = 2, kGroupWarps = 4, kMaxGroups = 2, kEpiWarp0 = 10, kEpiW = 4,
-              kBWarp = 14;
-constexpr int kThreads = 32 * (kBWarp + 1);
-constexpr uint32_t kEpiBytes = kEpiW * 32 * kEpiStride * 4;
-
-struct Params {
-  const uint8_t *wimg;   // pointwise images [n tile][slab], b_bytes each
-  const uint8_t *dwblk;  // [slab][KS*KS + 1][slab_c] f32: taps, then bias
-  EpiArgs epi;           // OH, OW: output spatial size
-  int *err;
-  int tiles_x, tiles_y, n_tiles, slabs, total;
-  int tw, th, iw, mid_act;
-  int sh, sg, b_res, ng;
-  uint32_t halo_bytes, dw_bytes, h_stage, g_stage, b_bytes, acc_stride, tmem_cols, bias_bytes;
-};
-
-struct Item {
-  int b, x0, y0, nt;
-};
-__device__ __forceinline__ Item decode(const Params &p, int t) {
-  Item it;
-  it.nt = t % p.n_tiles;
-  int q = t / p.n_tiles;
-  const int tx = q % p.tiles_x;
-  q /= p.tiles_x;
-  const int ty = q % p.tiles_y;
-  it.b = q / p.tiles_y;
-  it.x0 = tx * p.tw;
-  it.y0 = ty * p.th;
-  return it;
-}
-
-// Four channels (group `cg`) of halo pixel R: the TMA wrote 128-byte rows with
-// the 16-byte chunk c of row R at chunk position c ^ (R & 7).
-__device__ __forceinline__ float4 halo_ld(const float *, const uint8_t *halo, int R, int cg) {
-  return *reinterpret_cast<const float4 *>(halo + R * 128 + ((cg ^ (R & 7)) << 4));
-}
-__device__ __forceinline__ float4 halo_ld(const __nv_bfloat16 *, const uint8_t *halo, int R, int cg) {
-  const uint2 v = *reinterpret_cast<const uint2 *>(halo + R * 128 + (((cg >> 1) ^ (R & 7)) << 4) + ((cg & 1) << 3));
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v.y));
-  return make_float4(a.x, a.y, b.x, b.y);
-}
-// Row r, channel group cg of the K-major SWIZZLE_128B A image(s).
-__device__ __forceinline__ void a_st(const float *, uint8_t *A, int r, int cg, float4 v) {
-  uint4 hi, lo;
-  split(v.x, hi.x, lo.x), split(v.y, hi.y, lo.y), split(v.z, hi.z, lo.z), split(v.w, hi.w, lo.w);
-  const int off = r * 128 + ((cg ^ (r & 7)) << 4);
-  *reinterpret_cast<uint4 *>(A + off) = hi;
-  *reinterpret_cast<uint4 *>(A + kAImage + off) = lo;
-}
-__device__ __forceinline__ void a_st(const __nv_bfloat16 *, uint8_t *A, int r, int cg, float4 v) {
-  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-  uint2 u;
-  u.x = *reinterpret_cast<uint32_t *>(&a);
-  u.y = *reinterpret_cast<uint32_t *>(&b);
-  *reinterpret_cast<uint2 *>(A + r * 128 + (((cg >> 1) ^ (r & 7)) << 4) + ((cg & 1) << 3)) = u;
-}
-
-// Depthwise of one slab for one item: halo + weights -> A image. `ct` is the
-// thread's index within its group of kGroupWarps warps.
-template <typename T, int KS, int S, int P, int ACT>
-__device__ __forceinline__ void depthwise_slab(const Params &p, const Item &it, const uint8_t *halo,
-                                               const float *dww, uint8_t *A, int ct) {
-  constexpr int kSlabC = 128 / (int)sizeof(T);
-  constexpr int kCG = kSlabC / 4;
-  constexpr int kSpan = (P - 1) * S + KS;
-  const int runs = p.tw / P;
-  const int units = p.th * runs * kCG;
-  const int OH = p.epi.OH, OW = p.epi.OW;
-  for (int u = ct; u < units; u += kGroupWarps * 32) {
-    const int cg = u % kCG;
-    const int q = u / kCG;
-    const int run = q % runs, ly = q / runs;
-    const int lx0 = run * P;
-    if (it.y0 + ly >= OH || it.x0 + lx0 >= OW) continue;
-    const float4 bias = *reinterpret_cast<const float4 *>(dww + KS * KS * kSlabC + cg * 4);
-    float4 acc[P];
-#pragma unroll
-    for (int pp = 0; pp < P; pp++) acc[pp] = bias;
-#pragma unroll
-    for (int ky = 0; ky < KS; ky++) {
-      float4 w[KS];
-#pragma unroll
-      for (int kx = 0; kx < KS; kx++)
-        w[kx] = *reinterpret_cast<const float4 *>(dww + (ky * KS + kx) * kSlabC + cg * 4);
-      const int R0 = (ly * S + ky) * p.iw + lx0 * S;
-#pragma unroll
-      for (int j = 0; j < kSpan; j++) {
-        const float4 x = halo_ld(static_cast<const T *>(nullptr), halo, R0 + j, cg);
-#pragma unroll
-        for (int pp = 0; pp < P; pp++) {
-          const int kx = j - pp * S;
-          if (kx >= 0 && kx < KS) acc[pp] = f4fma(x, w[kx], acc[pp]);
-        }
-      }
-    }
-    const int nvalid = min(P, OW - (it.x0 + lx0));
-#pragma unroll
-    for (int pp = 0; pp < P; pp++)
-      if (pp < nvalid) a_st(static_cast<const T *>(nullptr), A, ly * p.tw + lx0 + pp, cg, act_c4<ACT>(acc[pp]));
-  }
-}
-
-template <typename T, int KS, int S, int P>
-__device__ __forceinline__ void depthwise_dispatch(const Params &p, const Item &it, const uint8_t *halo,
-                                                   const float *dww, uint8_t *A, int ct) {
-  switch (p.mid_act) {
-    case 1: depthwise_slab<T, KS, S, P, 1>(p, it, halo, dww, A, ct); break;
-    case 2: depthwise_slab<T, KS, S, P, 2>(p, it, halo, dww, A, ct); break;
-    case 3: depthwise_slab<T, KS, S, P, 3>(p, it, halo, dww, A, ct); break;
-    default: depthwise_slab<T, KS, S, P, 0>(p, it, halo, dww, A, ct); break;
-  }
-}
-
-template <typename T, int KS, int S, int P>
-__global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ CUtensorMap tmap, const Params p) {
-  constexpr bool kF32 = sizeof(T) == 4;
-  constexpr int kTerms = kF32 ? 2 : 1;
-  constexpr int kSlabC = 128 / (int)sizeof(T);
-  constexpr int kPad = (KS - 1) / 2;
-
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  uint8_t *base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t *hbase = base;
-  uint8_t *gbase = hbase + p.sh * p.h_stage;
-  uint8_t *bres = gbase + p.sg * p.g_stage;
-  const uint32_t res_bytes = p.b_res ? (uint32_t)(p.n_tiles * p.slabs) * p.b_bytes : 0u;
-  float *epi_smem = reinterpret_cast<float *>(bres + res_bytes);
-  float *bias_smem = epi_smem + kEpiBytes / 4;
-  uint64_t *h_full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(bias_smem) + p.bias_bytes);
-  uint64_t *h_empty = h_full + p.sh;
-  uint64_t *g_full = h_empty + p.sh;
-  uint64_t *a_ready = g_full + p.sg;
-  uint64_t *g_empty = a_ready + p.sg;
-  uint64_t *acc_full = g_empty + p.sg;
-  uint64_t *acc_empty = acc_full + 2;
-  uint64_t *b_full = acc_empty + 2;
-  uint64_t *drain = b_full + 1;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_tile = p.epi.n_tile;
-  if (tid == 0) {
-    for (int s = 0; s < p.sh; s++) {
-      mbar_init(&h_full[s], 1);
-      mbar_init(&h_empty[s], kGroupWarps);
-    }
-    for (int s = 0; s < p.sg; s++) {
-      mbar_init(&g_full[s], 1);
-      mbar_init(&a_ready[s], kGroupWarps);
-      mbar_init(&g_empty[s], 1);
-    }
-    for (int a = 0; a < 2; a++) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpiW);
-    }
-    mbar_init(b_full, 1);
-    mbar_init(drain, 1);
-    fence_barrier_init();
-  }
-  for (int i = tid; i < p.epi.N; i += kThreads) bias_smem[i] = p.epi.bias[i];
-  if (warp == 0) tmem_alloc(tmem_slot, p.tmem_cols);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  bool ok = true;
-
-  if (warp == 0) {
-    // ------------------------------------------------------- halo producer
-    if (lane == 0) {
-      int hs = 0;
-      uint32_t hph = 0;
-      long issued = 0;
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
-        const Item it = decode(p, t);
-        for (int s = 0; s < p.slabs; s++) {
-          if (!mbar_wait(&h_empty[hs], hph ^ 1u)) {
-            ok = false;
-            break;
-          }
-          uint8_t *hst = hbase + (size_t)hs * p.h_stage;
-          mbar_expect_tx(&h_full[hs], p.halo_bytes + p.dw_bytes);
-          tma_load_4d(smem_u32(hst), &tmap, s * kSlabC, it.x0 * S - kPad, it.y0 * S - kPad, it.b, &h_full[hs]);
-          bulk_load(smem_u32(hst + p.halo_bytes), p.dwblk + (size_t)s * p.dw_bytes, p.dw_bytes, &h_full[hs]);
-          issued++;
-          if (++hs == p.sh) hs = 0, hph ^= 1u;
-        }
-      }
-      // every copy issued above lands before the CTA may leave
-      for (long i = issued > p.sh ? issued - p.sh : 0; i < issued; i++)
-        ok = mbar_wait(&h_full[i % p.sh], (uint32_t)((i / p.sh) & 1)) && ok;
-    }
-  } else if (warp == kBWarp) {
-    // ------------------------------------------------------- weight producer
-    if (lane == 0) {
-      if (p.b_res) {
-        mbar_expect_tx(b_full, res_bytes);
-        for (int i = 0; i < p.n_tiles * p.slabs; i++)
-          bulk_load(smem_u32(bres + (size_t)i * p.b_bytes), p.wimg + (size_t)i * p.b_bytes, p.b_bytes, b_full);
-        ok = mbar_wait(b_full, 0);
-      } else {
-        int gs = 0;
-        uint32_t gph = 0;
-        long issued = 0;
-        for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
-          const int nt = t % p.n_tiles;
-          for (int s = 0; s < p.slabs; s++) {
-            if (!mbar_wait(&g_empty[gs], gph ^ 1u)) {
-              ok = false;
-              break;
-            }
-            mbar_expect_tx(&g_full[gs], p.b_bytes);
-            bulk_load(smem_u32(gbase + (size_t)gs * p.g_stage + kTerms * kAImage),
-                      p.wimg + ((size_t)nt * p.slabs + s) * p.b_bytes, p.b_bytes, &g_full[gs]);
-            issued++;
-            if (++gs == p.sg) gs = 0, gph ^= 1u;
-          }
-        }
-        for (long i = issued > p.sg ? issued - p.sg : 0; i < issued; i++)
-          ok = mbar_wait(&g_full[i % p.sg], (uint32_t)((i / p.sg) & 1)) && ok;
-      }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      if (p.b_res && !mbar_wait(b_full, 0)) ok = false;
-      int gs = 0, acc = 0;
-      uint32_t gph = 0, acc_phase = 0;
-      const uint32_t idesc = instr_desc(kF32 ? 2u : 1u, (uint32_t)n_tile);
-      const uint32_t b_img = (uint32_t)n_tile * 128u;
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
-        const int nt = t % p.n_tiles;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)acc * p.acc_stride;
-        for (int s = 0; s < p.slabs; s++) {
-          if (!mbar_wait(&a_ready[gs], gph) || (!p.b_res && !mbar_wait(&g_full[gs], gph))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(gbase + (size_t)gs * p.g_stage);
-          const uint32_t sb = p.b_res ? smem_u32(bres + ((size_t)nt * p.slabs + s) * p.b_bytes) : sa + kTerms * kAImage;
-          mma_slab<kF32>(d, sa, sa + kAImage, sb, sb + b_img, idesc, s == 0);
-          mma_commit(&g_empty[gs]);
-          if (++gs == p.sg) gs = 0, gph ^= 1u;
-        }
-        if (!ok) break;
-        mma_commit(&acc_full[acc]);
-        if (++acc == 2) acc = 0, acc_phase ^= 1u;
-      }
-      // no MMA of this thread is in flight once `drain` completes
-      mma_commit(drain);
-      if (!mbar_wait(drain, 0)) ok = false;
-    }
-  } else if (warp < kEpiWarp0) {
-    // ------------------------------------------------------- depthwise
-    const int grp = (warp - kXfWarp0) / kGroupWarps;
-    const int ct = tid - (kXfWarp0 + grp * kGroupWarps) * 32;
-    if (grp < p.ng) {
-      long q = 0;  // (item, slab) step index of this CTA
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
-        const Item it = decode(p, t);
-        for (int s = 0; s < p.slabs; s++, q++) {
-          if ((int)(q % p.ng) != grp) continue;
-          const int hs = (int)(q % p.sh), gs = (int)(q % p.sg);
-          const uint32_t hph = (uint32_t)((q / p.sh) & 1), gph = (uint32_t)((q / p.sg) & 1);
-          if (!__all_sync(0xffffffffu, mbar_wait(&h_full[hs], hph)) ||
-              !__all_sync(0xffffffffu, mbar_wait(&g_empty[gs], gph ^ 1u))) {
-            ok = false;
-            break;
-          }
-          const uint8_t *hst = hbase + (size_t)hs * p.h_stage;
-          depthwise_dispatch<T, KS, S, P>(p, it, hst, reinterpret_cast<const float *>(hst + p.halo_bytes),
-                                          gbase + (size_t)gs * p.g_stage, ct);
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&a_ready[gs]);
-            mbar_arrive(&h_empty[hs]);
-          }
-        }
-      }
-    }
-  } else {
-    // ------------------------------------------------------- epilogue
-    const int e = warp - kEpiWarp0;
-    const int lane_base = (warp & 3) * 32;
-    float *blk = epi_smem + e * 32 * kEpiStride;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    const int tw = p.tw, th = p.th, OH = p.epi.OH, OW = p.epi.OW;
-    EpiArgs ea = p.epi;
-    ea.bias = bias_smem;
-    for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
-      const Item it = decode(p, t);
-      uint64_t *full = &acc_full[acc];
-      const uint32_t ph = acc_phase;
-      if (!epilogue_rows<T, 0>(
-              ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base, 0, n_tile,
-              it.nt * n_tile, blk,
-              [=](int r) -> long {
-                const int ly = r / tw, lx = r - ly * tw;
-                const int y = it.y0 + ly, x = it.x0 + lx;
-                if (ly >= th || y >= OH || x >= OW) return -1;
-                return ((long)it.b * OH + y) * OW + x;
-              },
-              [full, ph]() {
-                const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph));
-                tc_fence_after();
-                return w;
-              })) {
-        ok = false;
-        break;
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      if (++acc == 2) acc = 0, acc_phase ^= 1u;
-    }
-  }
-
-  if (!ok && p.err) atomicExch(p.err, 1);
-  __syncwarp();  // lanes that idled while lane 0 worked rejoin before the block barrier
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, p.tmem_cols);
-}
 
 // [K*K][C] packed depthwise taps + [C] bias -> per slab blocks of
 // (K*K + 1) rows x slab_c floats, zero past C.
@@ -403,6 +69,17 @@ __global__ void k_pack_dw_slabs(const float *dw_w, const float *dw_b, int C, int
   out[i] = ch < C ? (t < kk ? dw_w[(long)t * C + ch] : dw_b[ch]) : 0.0f;
 }
 
+
+// Instantiated in tc_dw_{f32,bf16}{,_split}.cu.
+extern template cudaError_t launch_all<float, false>(int, int, int, const CUtensorMap &, const Params &, size_t,
+                                                     cudaStream_t);
+extern template cudaError_t launch_all<float, true>(int, int, int, const CUtensorMap &, const Params &, size_t,
+                                                    cudaStream_t);
+extern template cudaError_t launch_all<__nv_bfloat16, false>(int, int, int, const CUtensorMap &, const Params &,
+                                                             size_t, cudaStream_t);
+extern template cudaError_t launch_all<__nv_bfloat16, true>(int, int, int, const CUtensorMap &, const Params &,
+                                                            size_t, cudaStream_t);
+
 }  // namespace tcd
 
 // ---------------------------------------------------------------------------
@@ -411,66 +88,91 @@ __global__ void k_pack_dw_slabs(const float *dw_w, const float *dw_b, int C, int
 
 namespace {
 
-constexpr size_t kSmemBudget = 227 * 1024;
+using tcd::kSmemBudget;
 
 size_t align_to(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// Bytes of one fp32 split-K partial tile of n_tile columns.
+double kTileMBytes(int n_tile) { return (double)tcx::kTileM * n_tile * 4; }
 
 struct DwTiling {
-  int tw = 0, th = 0, P = 0, iw = 0, ih = 0, sh = 0, sg = 0, b_res = 0, ng = 0;
+  int tw = 0, th = 0, P = 0, iw = 0, ih = 0, sh = 0, sg = 0, b_res = 0, ng = 0, ksplit = 1, spk = 0;
   size_t smem = 0;
   double cost = 0;
 };
 
-// Patch shape, depthwise groups, ring depths and weight residency for one op,
-// by a per-SM cycle estimate. Per (item, slab): a depthwise group needs the
-// halo copy (~1500 cycles of latency plus 64 B/cycle) and its arithmetic
-// (~6 cycles per instruction of one warp: the groups are latency bound),
-// overlapped when the group owns two H stages and serialised otherwise; `ng`
-// groups interleave; the MMAs (fp32: 16 TF32 MMAs) and the halo bandwidth
-// bound the step from below. The epilogue of an item overlaps the next item.
-DwTiling plan_tiling(int T, int OH, int OW, int KS, int S, const TcWeights &w, bool has_res) {
-  const size_t bias_bytes = align_to((size_t)w.N * 4, 16);
+// Patch shape, run length P, depthwise groups, ring depths, weight residency
+// and K split for one launch, by a per-SM cycle estimate of the launch's wall
+// time: units (item x K split) spread over the SMs in waves; per (unit, slab)
+// a depthwise group needs the halo copy (~1500 cycles of latency plus 64 B per
+// cycle) and its arithmetic (~6 cycles per instruction of one warp: the groups
+// are latency bound), overlapped when the group owns two H stages and
+// serialised otherwise; `ng` groups interleave; the MMAs, the halo bandwidth
+// and the shared-memory wavefronts (depthwise loads and stores, UMMA operand
+// reads, TMA writes) bound the step from below. A split item adds the partial
+// tile store and, on the CTA that finishes it, the reduction.
+DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const TcWeights &w, bool has_res,
+                     size_t ws_bytes, int cnt_n) {
   const bool f32 = T == F32;
+  const size_t bias_bytes = align_to((size_t)w.N * 4, 16);
   const int terms = f32 ? 2 : 1, slab_c = f32 ? 32 : 64, cgs = slab_c / 4;
   const size_t dw_bytes = (size_t)(KS * KS + 1) * slab_c * 4;
   const size_t a_bytes = (size_t)terms * tcx::kAImage, b_bytes = (size_t)terms * w.n_tile * 128;
   const size_t res_total = (size_t)w.n_tiles * w.slabs * b_bytes;
   const double mma = f32 ? 1000.0 + 8.0 * w.n_tile : 300.0 + 2.0 * w.n_tile;
+  const double mma_rd = f32 ? 512.0 + 4.0 * w.n_tile : 128.0 + 1.0 * w.n_tile;
   const double epi = (w.n_tile / 16.0) * (has_res ? 1400.0 : 700.0);
+  const double G = sm_count();
   DwTiling best;
-  const int Ps[3] = {8, 7, 4};
+  const int Ps[4] = {8, 7, 4, 2};
   for (int P : Ps) {
     for (int tw = P; tw <= 128 && tw < OW + P; tw += P) {
       const int iw = (tw - 1) * S + KS;
       if (iw > 256) break;
-      const int th_max = 128 / tw;
-      const int tiles_y = (OH + th_max - 1) / th_max;
-      const int th = (OH + tiles_y - 1) / tiles_y;
-      const int ih = (th - 1) * S + KS;
-      if (ih > 256) continue;
-      const double tiles = (double)((OW + tw - 1) / tw) * tiles_y;
-      const size_t halo = (size_t)iw * ih * 128;
-      const size_t h_stage = align_to(halo + dw_bytes, 1024);
-      const int units = th * (tw / P) * cgs;
-      const int rounds = (units + tcd::kGroupWarps * 32 - 1) / (tcd::kGroupWarps * 32);
-      const double xf = 6.0 * rounds * (KS * (4.0 * P * KS + (P - 1) * S + 2 * KS) + 40.0 * P);
-      const double lat = 1500.0 + halo / 64.0, bw = halo / 64.0;
-      for (int b_res = 1; b_res >= 0; b_res--) {
-        const size_t g_stage = a_bytes + (b_res ? 0 : b_bytes);
-        for (int ng = tcd::kMaxGroups; ng >= 1; ng--) {
-          for (int sh = ng; sh <= 4; sh += ng) {
-            for (int sg = ng; sg <= 4; sg += ng) {
-              const size_t smem = 1024 + sh * h_stage + sg * g_stage + (b_res ? res_total : 0) + tcd::kEpiBytes +
-                                  bias_bytes + 8 * (2 * sh + 3 * sg + 6) + 16;
-              if (smem > kSmemBudget) continue;
-              double group = sh / ng >= 2 ? std::fmax(lat, xf) : lat + xf;
-              if (sg / ng < 2) group += mma;
-              const double per_slab = std::fmax(std::fmax(group / ng, mma), bw);
-              const double per_item = std::fmax(w.slabs * per_slab, epi);
-              const double cost = tiles * w.n_tiles * per_item * (b_res ? 0.99 : 1.0) * (1.0 - 0.001 * (sh + sg));
-              if (best.tw == 0 || cost < best.cost) {
-                best.tw = tw, best.th = th, best.P = P, best.iw = iw, best.ih = ih, best.ng = ng;
-                best.sh = sh, best.sg = sg, best.b_res = b_res, best.smem = smem, best.cost = cost;
+      for (int th_div = 1; th_div <= 4; th_div *= 2) {
+        const int th_max = std::max(1, 128 / tw / th_div);
+        if (th_div > 1 && th_max == std::max(1, 128 / tw / (th_div / 2))) continue;
+        const int tiles_y = (OH + th_max - 1) / th_max;
+        const int th = (OH + tiles_y - 1) / tiles_y;
+        const int ih = (th - 1) * S + KS;
+        if (ih > 256) continue;
+        const double items = (double)n_frames * ((OW + tw - 1) / tw) * tiles_y * w.n_tiles;
+        const size_t halo = (size_t)iw * ih * 128;
+        const size_t h_stage = align_to(halo + dw_bytes, 1024);
+        const int units = th * (tw / P) * cgs;
+        const int rounds = (units + tcd::kGroupWarps * 32 - 1) / (tcd::kGroupWarps * 32);
+        const int span = (P - 1) * S + KS;
+        const double xf = 6.0 * rounds * (KS * (4.0 * P * KS + span + KS) + 40.0 * P);
+        const double lat = 1500.0 + halo / 64.0, bw = halo / 64.0;
+        const double smem_rd = units / 8.0 * KS * (span + KS) + units * P * terms / 8.0 + mma_rd + iw * ih;
+        for (int b_res = 1; b_res >= 0; b_res--) {
+          const size_t g_stage = a_bytes + (b_res ? 0 : b_bytes);
+          for (int ng = tcd::kMaxGroups; ng >= 1; ng--) {
+            for (int sh = ng; sh <= 4; sh += ng) {
+              for (int sg = ng; sg <= 4; sg += ng) {
+                const size_t smem = 1024 + sh * h_stage + sg * g_stage + (b_res ? res_total : 0) + tcd::kEpiBytes +
+                                    bias_bytes + 8 * (2 * sh + 3 * sg + 6) + 16;
+                if (smem > kSmemBudget) continue;
+                double group = sh / ng >= 2 ? std::fmax(lat, xf) : lat + xf;
+                if (sg / ng < 2) group += mma;
+                const double per_slab = std::fmax(std::fmax(group / ng, mma), std::fmax(bw, smem_rd));
+                int last_ks = 0;
+                for (int want = 1; want <= std::min(w.slabs, 16); want++) {
+                  const int spk = (w.slabs + want - 1) / want;
+                  const int ks = (w.slabs + spk - 1) / spk;
+                  if (ks == last_ks) continue;
+                  last_ks = ks;
+                  if (ks > 1 && (items * ks * kTileMBytes(w.n_tile) > (double)ws_bytes || items > cnt_n)) break;
+                  const double nunits = items * ks;
+                  const double waves = std::ceil(nunits / G);
+                  const double per_unit = std::fmax(spk * per_slab, epi) + (ks > 1 ? 600.0 : 0.0);
+                  const double red = ks > 1 ? 1500.0 + ks * 128.0 * w.n_tile * 4 / 32.0 + epi : 0.0;
+                  const double cost = (waves * per_unit + red) * (b_res ? 0.99 : 1.0) * (1.0 - 0.001 * (sh + sg));
+                  if (best.tw == 0 || cost < best.cost) {
+                    best.tw = tw, best.th = th, best.P = P, best.iw = iw, best.ih = ih, best.ng = ng;
+                    best.sh = sh, best.sg = sg, best.b_res = b_res, best.smem = smem, best.cost = cost;
+                    best.ksplit = ks, best.spk = spk;
+                  }
+                }
               }
             }
           }
@@ -481,40 +183,19 @@ DwTiling plan_tiling(int T, int OH, int OW, int KS, int S, const TcWeights &w, b
   return best;
 }
 
-template <typename T, int KS, int S, int P>
-cudaError_t launch_dw(const CUtensorMap &map, const tcd::Params &p, size_t smem, cudaStream_t st) {
-  auto kern = tcd::k_tc_dw<T, KS, S, P>;
-  static unsigned long long granted = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !(granted & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget);
-    if (e != cudaSuccess) return e;
-    granted |= 1ull << dev;
-  }
-  const unsigned grid = (unsigned)(p.total < sm_count() ? p.total : sm_count());
-  kern<<<grid, tcd::kThreads, smem, st>>>(map, p);
-  return cudaGetLastError();
-}
-
-template <typename T, int KS, int S>
-cudaError_t launch_p(int P, const CUtensorMap &map, const tcd::Params &p, size_t smem, cudaStream_t st) {
-  switch (P) {
-    case 8: return launch_dw<T, KS, S, 8>(map, p, smem, st);
-    case 7: return launch_dw<T, KS, S, 7>(map, p, smem, st);
-    case 4: return launch_dw<T, KS, S, 4>(map, p, smem, st);
-    default: return cudaErrorInvalidValue;
-  }
-}
-
-template <typename T>
-cudaError_t launch_t(int KS, int S, int P, const CUtensorMap &map, const tcd::Params &p, size_t smem,
-                     cudaStream_t st) {
-  if (KS == 3 && S == 1) return launch_p<T, 3, 1>(P, map, p, smem, st);
-  if (KS == 3 && S == 2) return launch_p<T, 3, 2>(P, map, p, smem, st);
-  if (KS == 5 && S == 1) return launch_p<T, 5, 1>(P, map, p, smem, st);
-  if (KS == 5 && S == 2) return launch_p<T, 5, 2>(P, map, p, smem, st);
-  return cudaErrorInvalidValue;
+// plan_tiling is a few-thousand-candidate search; launches of one shape reuse it.
+DwTiling cached_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const TcWeights &w, bool has_res,
+                       size_t ws_bytes, int cnt_n) {
+  using Key = std::array<long, 12>;
+  static std::mutex mu;
+  static std::map<Key, DwTiling> cache;
+  const Key key{T, n_frames, OH, OW, KS, S, w.N, w.K, has_res ? 1 : 0, (long)ws_bytes, cnt_n, sm_count()};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  const DwTiling t = plan_tiling(T, n_frames, OH, OW, KS, S, w, has_res, ws_bytes, cnt_n);
+  cache.emplace(key, t);
+  return t;
 }
 
 }  // namespace
@@ -545,7 +226,8 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   if ((op.ks != 3 && op.ks != 5) || (op.stride != 1 && op.stride != 2)) return cudaErrorInvalidValue;
   auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
-  const DwTiling tl = plan_tiling(T, op.OH, op.OW, op.ks, op.stride, plan, op.res != nullptr);
+  const DwTiling tl = cached_tiling(T, op.n, op.OH, op.OW, op.ks, op.stride, plan, op.res != nullptr,
+                                    op.ws ? op.ws_bytes : 0, op.ws_cnt ? op.ws_cnt_n : 0);
   if (tl.tw == 0) return cudaErrorInvalidValue;
 
   const size_t elt = T == F32 ? 4 : 2;
@@ -570,9 +252,11 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.tiles_x = (op.OW + tl.tw - 1) / tl.tw;
   p.tiles_y = (op.OH + tl.th - 1) / tl.th;
   p.n_tiles = plan.n_tiles, p.slabs = plan.slabs;
-  const long total = (long)op.n * p.tiles_x * p.tiles_y * plan.n_tiles;
+  const long items = (long)op.n * p.tiles_x * p.tiles_y * plan.n_tiles;
+  const long total = items * tl.ksplit;
   if (total > 0x7fffffffL) return cudaErrorInvalidValue;
-  p.total = (int)total;
+  p.items = (int)items, p.ksplit = tl.ksplit, p.spk = tl.spk, p.total = (int)total;
+  p.ws = op.ws, p.cnt = op.ws_cnt;
   p.tw = tl.tw, p.th = tl.th, p.iw = tl.iw, p.mid_act = op.mid_act;
   p.sh = tl.sh, p.sg = tl.sg, p.b_res = tl.b_res, p.ng = tl.ng;
   p.halo_bytes = (uint32_t)(tl.iw * tl.ih * 128);
@@ -584,8 +268,12 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   while ((int)p.acc_stride < plan.n_tile) p.acc_stride <<= 1;
   p.tmem_cols = 2 * p.acc_stride;
   p.bias_bytes = (uint32_t)align_to((size_t)op.N * 4, 16);
-  if (T == F32) return launch_t<float>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
-  return launch_t<__nv_bfloat16>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
+  const bool split = tl.ksplit > 1;
+  if (T == F32)
+    return split ? tcd::launch_all<float, true>(op.ks, op.stride, tl.P, map, p, tl.smem, st)
+                 : tcd::launch_all<float, false>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
+  return split ? tcd::launch_all<__nv_bfloat16, true>(op.ks, op.stride, tl.P, map, p, tl.smem, st)
+               : tcd::launch_all<__nv_bfloat16, false>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
 }
 
 }  // namespace gpu

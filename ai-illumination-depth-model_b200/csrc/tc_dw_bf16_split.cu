@@ -1,0 +1,12 @@
+// Instances of the depthwise -> pointwise tcgen05 kernel (tc_dw_kernel.cuh)
+// for bf16 storage, split-K launches.
+#include "tc_dw_kernel.cuh"
+
+namespace illumina {
+namespace gpu {
+namespace tcd {
+template cudaError_t launch_all<__nv_bfloat16, true>(int, int, int, const CUtensorMap &, const Params &, size_t,
+                                                         cudaStream_t);
+}  // namespace tcd
+}  // namespace gpu
+}  // namespace illumina
