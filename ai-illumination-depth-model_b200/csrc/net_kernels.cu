@@ -19,6 +19,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "pdl.cuh"
 
 namespace illumina {
 namespace gpu {
@@ -103,6 +104,8 @@ constexpr long kMaxIndex = 0x7fffffffL;
 template <typename T>
 __global__ void k_preprocess(const float *__restrict__ frames, int layout, long total, int S, PreprocessParams p,
                              T *__restrict__ input, float *__restrict__ luma, float *__restrict__ scene) {
+  pdl_wait();
+  pdl_trigger();
   long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   long plane = (long)S * S;
@@ -131,12 +134,10 @@ cudaError_t preprocess(int T, const float *frames, int layout, int n, int S, con
   if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
   if (T == F32)
-    k_preprocess<float><<<blocks_for(total, 256), 256, 0, st>>>(frames, layout, total, S, p, (float *)input, luma,
-                                                                scene);
-  else
-    k_preprocess<__nv_bfloat16><<<blocks_for(total, 256), 256, 0, st>>>(frames, layout, total, S, p,
-                                                                         (__nv_bfloat16 *)input, luma, scene);
-  return cudaGetLastError();
+    return launch_pdl(k_preprocess<float>, dim3(blocks_for(total, 256)), dim3(256), 0, st, frames, layout, total, S, p,
+                      (float *)input, luma, scene);
+  return launch_pdl(k_preprocess<__nv_bfloat16>, dim3(blocks_for(total, 256)), dim3(256), 0, st, frames, layout, total,
+                    S, p, (__nv_bfloat16 *)input, luma, scene);
 }
 
 // ---------------------------------------------------------------------------
@@ -147,6 +148,8 @@ template <typename T>
 __global__ void k_conv(const T *__restrict__ src, int n, int H, int W, int Cin, const float *__restrict__ wpk,
                        const float *__restrict__ bias, int Cout, int k, int stride, int act, int OH, int OW,
                        T *__restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
   long pix = (long)blockIdx.x * blockDim.x + threadIdx.x;
   long total = (long)n * OH * OW;
   if (pix >= total) return;
@@ -206,12 +209,10 @@ cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const flo
   if (total <= 0) return cudaSuccess;
   dim3 grid(blocks_for(total, 128), (Cout / 4 + 3) / 4);
   if (T == F32)
-    k_conv<float><<<grid, 128, 0, st>>>((const float *)src, n, H, W, Cin, wpk, bias, Cout, k, stride, act, OH, OW,
-                                        (float *)dst);
-  else
-    k_conv<__nv_bfloat16><<<grid, 128, 0, st>>>((const __nv_bfloat16 *)src, n, H, W, Cin, wpk, bias, Cout, k, stride,
-                                                act, OH, OW, (__nv_bfloat16 *)dst);
-  return cudaGetLastError();
+    return launch_pdl(k_conv<float>, grid, dim3(128), 0, st, (const float *)src, n, H, W, Cin, wpk, bias, Cout, k,
+                      stride, act, OH, OW, (float *)dst);
+  return launch_pdl(k_conv<__nv_bfloat16>, grid, dim3(128), 0, st, (const __nv_bfloat16 *)src, n, H, W, Cin, wpk, bias,
+                    Cout, k, stride, act, OH, OW, (__nv_bfloat16 *)dst);
 }
 
 // ---------------------------------------------------------------------------
@@ -236,6 +237,8 @@ struct GemmParams {
 // MODE 0: pointwise; 1: depthwise KS x KS then pointwise; 2: lateral
 template <typename T, int BM, int BN, int MODE, int KS>
 __global__ void __launch_bounds__(GTHREADS) k_gemm(const GemmParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int TM = BM / 16, TN = BN / 16;
   constexpr int A_VEC = BM * 4;  // float4 groups per chunk (BM pixels x 4 channel groups)
   constexpr int A_PER = (A_VEC + GTHREADS - 1) / GTHREADS;
@@ -418,8 +421,7 @@ static cudaError_t launch_gemm_t(const GemmParams &p, cudaStream_t st) {
   dim3 grid((unsigned)((p.M + bm - 1) / bm), (unsigned)((p.N + bn - 1) / bn));
 #define ILL_GEMM_CASE(BM_, BN_)                                      \
   if (bm == BM_ && bn == BN_) {                                      \
-    k_gemm<T, BM_, BN_, MODE, KS><<<grid, GTHREADS, 0, st>>>(p);     \
-    return cudaGetLastError();                                       \
+    return launch_pdl(k_gemm<T, BM_, BN_, MODE, KS>, grid, dim3(GTHREADS), 0, st, p); \
   }
   ILL_GEMM_CASE(128, 32) ILL_GEMM_CASE(64, 32) ILL_GEMM_CASE(32, 32)
   ILL_GEMM_CASE(128, 64) ILL_GEMM_CASE(64, 64) ILL_GEMM_CASE(32, 64)
@@ -454,6 +456,8 @@ cudaError_t gemm(int T, const GemmOp &op, cudaStream_t st) {
 template <typename T>
 __global__ void k_head(const T *__restrict__ src, long M, int C, const float *__restrict__ w, float bias,
                        float *__restrict__ dst1, float *__restrict__ dst4) {
+  pdl_wait();
+  pdl_trigger();
   long m = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= M) return;
   float s = bias;
@@ -475,11 +479,10 @@ cudaError_t head(int T, const void *src, long M, int C, const float *w, float bi
                  cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   if (T == F32)
-    k_head<float><<<blocks_for(M, 256), 256, 0, st>>>((const float *)src, M, C, w, bias, dst1, dst4);
-  else
-    k_head<__nv_bfloat16><<<blocks_for(M, 256), 256, 0, st>>>((const __nv_bfloat16 *)src, M, C, w, bias, dst1,
-                                                              dst4);
-  return cudaGetLastError();
+    return launch_pdl(k_head<float>, dim3(blocks_for(M, 256)), dim3(256), 0, st, (const float *)src, M, C, w, bias,
+                      dst1, dst4);
+  return launch_pdl(k_head<__nv_bfloat16>, dim3(blocks_for(M, 256)), dim3(256), 0, st, (const __nv_bfloat16 *)src, M, C,
+                    w, bias, dst1, dst4);
 }
 
 // ---------------------------------------------------------------------------
@@ -493,6 +496,8 @@ __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh
                             const float *__restrict__ luma, const float *__restrict__ guide, int gc,
                             BilateralParams p, float *__restrict__ dst, const float *__restrict__ history,
                             float *__restrict__ out_tex) {
+  pdl_wait();
+  pdl_trigger();
   int S = lh * 2, SW = lw * 2;
   long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   long total = (long)n * S * SW;
@@ -541,9 +546,8 @@ cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *lum
   long total = (long)n * lh * lw * 4;
   if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
-  k_bilateral<<<blocks_for(total, 256), 256, 0, st>>>(low1, 1, n, lh, lw, luma, nullptr, 0, p, dst, history,
-                                                      out_tex);
-  return cudaGetLastError();
+  return launch_pdl(k_bilateral, dim3(blocks_for(total, 256)), dim3(256), 0, st, low1, 1, n, lh, lw, luma,
+                    (const float *)nullptr, 0, p, dst, history, out_tex);
 }
 
 cudaError_t bilateral_strided(const float *low, int lh, int lw, int low_c, const float *guide, int guide_c,

@@ -370,8 +370,11 @@ __device__ __forceinline__ bool epilogue_body(const EpiArgs &a, uint32_t tacc_la
 
 // Split-K: writes the fp32 accumulator columns [0, ncols) of this warp's 32
 // TMEM lanes as rows lane_base + lane of a [128][ld] partial tile (no bias,
-// no activation). Bypasses L1: another SM reads the tile.
-__device__ __forceinline__ void store_partial(uint32_t tacc_lane, int lane_base, int ncols, float *tile, int ld) {
+// no activation); warps whose rows all lie past `rows_valid` write nothing.
+// Bypasses L1: another SM reads the tile.
+__device__ __forceinline__ void store_partial(uint32_t tacc_lane, int lane_base, int ncols, float *tile, int ld,
+                                              int rows_valid) {
+  if (lane_base >= rows_valid) return;  // warp-uniform: rows past the patch are padding
   const int lane = threadIdx.x & 31;
   float *row = tile + (size_t)(lane_base + lane) * ld;
   for (int cb = 0; cb < ncols; cb += kEpiCols) {
@@ -388,58 +391,71 @@ __device__ __forceinline__ void store_partial(uint32_t tacc_lane, int lane_base,
   }
 }
 
+// Split-K: output pixel of tile row r of an output patch (th x tw pixels at
+// (x0, y0) of frame b), or -1 for a padding row.
+struct PatchMap {
+  int b, x0, y0, tw, th, OH, OW;
+  __device__ __forceinline__ long operator()(int r) const {
+    const int ly = r / tw, lx = r - ly * tw;
+    const int y = y0 + ly, x = x0 + lx;
+    if (ly >= th || y >= OH || x >= OW) return -1;
+    return ((long)b * OH + y) * OW + x;
+  }
+};
+
 // Split-K: sums the ksplit partial tiles of one item ([ksplit][128][ld] at
-// `part`, split order fixed so the result does not depend on which CTA
-// finished last), then bias, residual, activation and store, for this warp's
-// rows and columns [0, ncols) (output columns n_base + c). Same lane layout as
-// epilogue_body; partials are read past L1 (written by other SMs).
+// `part`; split order fixed, so the result does not depend on which CTA
+// finished last), then bias, residual, activation and store. The nw calling
+// warps (warp index wi) share (8-row group, 16-column block) units; groups
+// beyond the patch's th*tw rows are skipped. Four splits' loads are in flight
+// at once; partials are read past L1 (written by other SMs).
 template <typename T, int ACT>
-__device__ __forceinline__ void reduce_body(const EpiArgs &a, const float *part, int ksplit, size_t split_stride,
-                                            int ld, int lane_base, int ncols, int n_base, const EpiRows &rows) {
+__device__ __forceinline__ void reduce_units(const EpiArgs &a, const float *part, int ksplit, size_t split_stride,
+                                             int ld, int ncols, int n_base, const PatchMap &pm, int wi, int nw) {
   const int lane = threadIdx.x & 31, chunk = lane & 3, rsub = lane >> 2;
   const T *res = reinterpret_cast<const T *>(a.res);
   T *dst = reinterpret_cast<T *>(a.dst);
-  for (int cb = 0; cb < ncols; cb += kEpiCols) {
-    const int c = cb + chunk * 4;
+  const int nblocks = (ncols + kEpiCols - 1) / kEpiCols;
+  const int ngroups = (pm.th * pm.tw + 7) / 8;
+  for (int u = wi; u < ngroups * nblocks; u += nw) {
+    const int rg = u / nblocks, blk = u - rg * nblocks;
+    const int r = rg * 8 + rsub;
+    const int c = blk * kEpiCols + chunk * 4;
     const int n = n_base + c;
-    if (chunk * 4 >= min(kEpiCols, ncols - cb) || n >= a.N) continue;
-    float4 o[4];
+    const long m = pm(r);
+    if (m < 0 || c >= ncols || n >= a.N) continue;
+    const float *pr = part + (size_t)r * ld + c;
+    float4 o = make_float4(0, 0, 0, 0);
+    for (int j = 0; j < ksplit; j += 4) {
+      float4 q[4];
 #pragma unroll
-    for (int i = 0; i < 4; i++) o[i] = make_float4(0, 0, 0, 0);
-    for (int j = 0; j < ksplit; j++) {
-      const float *pj = part + j * split_stride + c;
+      for (int k = 0; k < 4; k++)
+        q[k] = j + k < ksplit ? __ldcg(reinterpret_cast<const float4 *>(pr + (j + k) * split_stride))
+                              : make_float4(0, 0, 0, 0);
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const float4 q = __ldcg(reinterpret_cast<const float4 *>(pj + (size_t)(lane_base + i * 8 + rsub) * ld));
-        o[i].x += q.x, o[i].y += q.y, o[i].z += q.z, o[i].w += q.w;
-      }
+      for (int k = 0; k < 4; k++)
+        if (j + k < ksplit) o.x += q[k].x, o.y += q[k].y, o.z += q[k].z, o.w += q[k].w;
     }
     const float4 bias = *reinterpret_cast<const float4 *>(a.bias + n);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      o[i].x += bias.x, o[i].y += bias.y, o[i].z += bias.z, o[i].w += bias.w;
-      if (res && rows.m[i] >= 0) {
-        const float4 q = ld4(res + rows.m[i] * a.N + n);
-        o[i].x += q.x, o[i].y += q.y, o[i].z += q.z, o[i].w += q.w;
-      }
+    o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
+    if (res) {
+      const float4 q = ld4(res + m * a.N + n);
+      o.x += q.x, o.y += q.y, o.z += q.z, o.w += q.w;
     }
-    act_n<ACT, 4>(o);
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      if (rows.m[i] >= 0) st4(dst + rows.m[i] * a.N + n, o[i]);
+    st4(dst + m * a.N + n, act_c4<ACT>(o));
   }
 }
 
 // Out of line: the reduction's registers stay out of the persistent loop that
-// calls it (inlined, they made the common unsplit path spill).
+// calls it.
 template <typename T>
 __device__ __noinline__ void epilogue_reduce(const EpiArgs a, const float *part, int ksplit, size_t split_stride, int ld,
-                                             int lane_base, int ncols, int n_base, const EpiRows rows) {
+                                             int ncols, int n_base, const PatchMap pm, int wi, int nw) {
   switch (a.act) {
-    case 1: reduce_body<T, 1>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
-    case 2: reduce_body<T, 2>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
-    case 3: reduce_body<T, 3>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
-    default: reduce_body<T, 0>(a, part, ksplit, split_stride, ld, lane_base, ncols, n_base, rows); break;
+    case 1: reduce_units<T, 1>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
+    case 2: reduce_units<T, 2>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
+    case 3: reduce_units<T, 3>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
+    default: reduce_units<T, 0>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
   }
 }
 

@@ -164,8 +164,13 @@ DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const 
                   if (ks > 1 && (items * ks * kTileMBytes(w.n_tile) > (double)ws_bytes || items > cnt_n)) break;
                   const double nunits = items * ks;
                   const double waves = std::ceil(nunits / G);
-                  const double per_unit = std::fmax(spk * per_slab, epi) + (ks > 1 ? 600.0 : 0.0);
-                  const double red = ks > 1 ? 1500.0 + ks * 128.0 * w.n_tile * 4 / 32.0 + epi : 0.0;
+                  // split: partial store per unit, and on the finishing CTA a
+                  // reduction whose (8-row, 16-column) units are latency bound
+                  // (four splits' loads in flight per unit, four warps)
+                  const double red_units = std::ceil(th * tw / 8.0) * std::ceil(w.n_tile / 16.0);
+                  const double per_unit = std::fmax(spk * per_slab, epi) + (ks > 1 ? 300.0 * w.n_tile / 16 : 0.0);
+                  const double red =
+                      ks > 1 ? 1500.0 + std::ceil(red_units / 4) * (std::ceil(ks / 4.0) * 700.0 + 150.0) : 0.0;
                   const double cost = (waves * per_unit + red) * (b_res ? 0.99 : 1.0) * (1.0 - 0.001 * (sh + sg));
                   if (best.tw == 0 || cost < best.cost) {
                     best.tw = tw, best.th = th, best.P = P, best.iw = iw, best.ih = ih, best.ng = ng;

@@ -45,6 +45,7 @@
 #include <cudaTypedefs.h>
 
 #include "kernels.h"
+#include "pdl.cuh"
 #include "tc_common.cuh"
 
 namespace illumina {
@@ -236,6 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     mbar_init(drain, 1);
     fence_barrier_init();
   }
+  if (tid == 0) pdl_trigger();
   for (int i = tid; i < p.epi.N; i += kThreads) bias_smem[i] = p.epi.bias[i];
   if (warp == 0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
   if (warp == 0) {
     // ------------------------------------------------------- halo producer
     if (lane == 0) {
+      pdl_wait();  // the input is the previous kernel's output
       int hs = 0;
       uint32_t hph = 0;
       long issued = 0;
@@ -376,6 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     const int tw = p.tw, th = p.th, OH = p.epi.OH, OW = p.epi.OW;
     EpiArgs ea = p.epi;
     ea.bias = bias_smem;
+    pdl_wait();  // residual reads, split-K workspace and stores follow the previous kernel
     auto pix_of = [=](const Item &it) {
       return [=](int r) -> long {
         const int ly = r / tw, lx = r - ly * tw;
@@ -419,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         }
         float *part = p.ws + (size_t)it.id * p.ksplit * tile_elems;
         store_partial(tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base, n_tile,
-                      part + it.split * tile_elems, n_tile);
+                      part + it.split * tile_elems, n_tile, th * tw);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -430,11 +434,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         bar_named(1, kEpiW * 32);
         if (*last_flag) {
           __threadfence();
-          EpiRows rows;
-          const auto pix = pix_of(it);
-#pragma unroll
-          for (int i = 0; i < 4; i++) rows.m[i] = pix(lane_base + i * 8 + (lane >> 2));
-          epilogue_reduce<T>(ea, part, p.ksplit, tile_elems, n_tile, lane_base, n_tile, it.nt * n_tile, rows);
+          const PatchMap pm{it.b, it.x0, it.y0, tw, th, OH, OW};
+          epilogue_reduce<T>(ea, part, p.ksplit, tile_elems, n_tile, n_tile, it.nt * n_tile, pm, e, kEpiW);
           if (warp == kEpiWarp0 && lane == 0) p.cnt[it.id] = 0;  // ready for the next launch
         }
         bar_named(1, kEpiW * 32);  // last_flag is rewritten for the next unit
@@ -464,8 +465,7 @@ cudaError_t launch_dw(const CUtensorMap &map, const tcd::Params &p, size_t smem,
     granted |= 1ull << dev;
   }
   const unsigned grid = (unsigned)(p.total < sm_count() ? p.total : sm_count());
-  kern<<<grid, tcd::kThreads, smem, st>>>(map, p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(tcd::kThreads), smem, st, map, p);
 }
 
 template <typename T, int KS, int S, bool SPLIT>

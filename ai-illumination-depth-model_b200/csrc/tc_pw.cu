@@ -26,6 +26,7 @@
 #include <cstring>
 
 #include "kernels.h"
+#include "pdl.cuh"
 #include "tc_common.cuh"
 
 namespace illumina {
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     }
     fence_barrier_init();
   }
+  if (tid == 0) pdl_trigger();
   for (int i = tid; i < p.epi.N; i += kThreads) bias_smem[i] = p.epi.bias[i];
   if (warp == 0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
@@ -93,6 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      pdl_wait();  // the A tiles are the previous kernel's output
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -180,6 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     uint32_t acc_phase = 0;
     EpiArgs ea = p.epi;
     ea.bias = bias_smem;
+    pdl_wait();  // residual / coarse reads and the stores follow the previous kernel
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
       const long m0 = (long)mt * kTileM;
@@ -259,8 +263,7 @@ cudaError_t launch(const CUtensorMap &map, const tcp::Params &p, size_t smem, cu
   }
   const long tiles = (long)p.m_tiles * p.n_tiles;
   const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
-  kern<<<grid, tcp::kThreads, smem, st>>>(map, p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(tcp::kThreads), smem, st, map, p);
 }
 
 }  // namespace
