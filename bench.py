@@ -55,6 +55,55 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
+class RankGroup:
+    """The only cross-rank operations of a run: a barrier around each timed
+    region and a max-reduce of elapsed times (frames are independent, so there
+    is no collective on the data path). `backend` is "nccl" on the GPU box
+    (tensors on `device`), "gloo" for the CPU tests; world 1 needs no group."""
+
+    def __init__(self, world: int, backend: str = "nccl", device=None, timeout_s: int = 300):
+        self.world = world
+        self.device = device
+        self.pg = False
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            kw = {"device_id": device} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=self.device or "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+            self.pg = False
+
+
+def frame_seed_base(rank: int, batch: int) -> int:
+    """Rank r generates frames with seeds [r*batch, (r+1)*batch): disjoint
+    frame ranges, so N ranks process N*batch distinct frames (weak scaling)."""
+    return rank * batch
+
+
+def aggregate_frames_per_s(world: int, batch: int, steps: int, ms_max: float) -> float:
+    """Whole-job throughput: frames of all ranks over the slowest rank's time."""
+    return world * batch * steps / (ms_max / 1000.0)
+
+
 # ---------------------------------------------------------------------------
 # measured peaks, clocks
 # ---------------------------------------------------------------------------
@@ -250,33 +299,15 @@ def run_ours(args, rank, local_rank, world):
     from illumina import _lib
 
     torch.cuda.set_device(local_rank)
-    pg = False
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-        pg = True
-
-    def barrier():
-        if pg:
-            import torch.distributed as dist
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if not pg:
-            return x
-        import torch.distributed as dist
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    ranks = RankGroup(world, "nccl", torch.device("cuda", local_rank))
+    barrier, max_over_ranks = ranks.barrier, ranks.max
 
     B = args.batch
     arch = illumina.buildArchitecture(SIZE)
     cost = illumina.costOf(arch)
     model = illumina.createDepthModel(arch, synthSeed=0, maxBatch=B, precision=args.precision, device=local_rank)
     frames = torch.empty((B, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
-    _lib.check(_lib.lib().illumina_generate_frames(1, rank * B, B, SIZE, frames.data_ptr(), None))
+    _lib.check(_lib.lib().illumina_generate_frames(1, frame_seed_base(rank, B), B, SIZE, frames.data_ptr(), None))
     disp = torch.empty((B, SIZE, SIZE), dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
     launches = model.stats.launches
@@ -298,7 +329,7 @@ def run_ours(args, rank, local_rank, world):
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms)
-    value = world * B * args.steps / (ms_max / 1000.0)
+    value = aggregate_frames_per_s(world, B, args.steps, ms_max)
     ms_per_step = ms_max / args.steps
     stats = model.stats
     launches = stats.launches
@@ -323,7 +354,7 @@ def run_ours(args, rank, local_rank, world):
         torch.cuda.synchronize()
         barrier()
         e_ms = max_over_ranks(ev0.elapsed_time(ev1))
-        e2e = {"value": world * B * e_steps / (e_ms / 1000.0), "unit": UNIT,
+        e2e = {"value": aggregate_frames_per_s(world, B, e_steps, e_ms), "unit": UNIT,
                "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
                "steps": e_steps, "path": "illumina_forward (C ABI), pinned host buffers"}
         del host_in, host_out
@@ -395,9 +426,7 @@ def run_ours(args, rank, local_rank, world):
             "per_op_ms": {k: round(v, 4) for k, v in per_op.items()} if per_op else None,
         }
         print(json.dumps(line), flush=True)
-    if pg:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    ranks.close()
     return 0
 
 
