@@ -200,6 +200,87 @@ __global__ void k_conv(const T *__restrict__ src, int n, int H, int W, int Cin, 
   }
 }
 
+// Same op with the 16-channel group's weights staged in shared memory
+// ([k*k*Cin] x 4 float4, broadcast reads) and two output pixels per thread,
+// so each weight read serves eight FMAs. Accumulation order per output is
+// that of k_conv (bias, then ky, kx, input channel).
+template <typename T>
+__global__ void k_conv_sw(const T *__restrict__ src, int n, int H, int W, int Cin, const float *__restrict__ wpk,
+                          const float *__restrict__ bias, int Cout, int k, int stride, int act, int OH, int OW,
+                          T *__restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float4 wsm[];
+  const int og = blockIdx.y, cout4 = Cout >> 2, cin4 = Cin >> 2, g0 = og * 4;
+  const int rows = k * k * Cin;
+  for (int i = threadIdx.x; i < rows * 4; i += blockDim.x) {
+    const int r = i >> 2, g = g0 + (i & 3);
+    wsm[i] = g < cout4 ? __ldg(reinterpret_cast<const float4 *>(wpk) + (long)r * cout4 + g) : make_float4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const long total = (long)n * OH * OW;
+  const long pix0 = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (pix0 >= total) return;
+  const int npx = pix0 + 1 < total ? 2 : 1;
+  const int pad = (k - 1) >> 1;
+  int ox[2], oy[2], ob[2];
+#pragma unroll
+  for (int u = 0; u < 2; u++) unflatten3(u < npx ? pix0 + u : pix0, OW, OH, ox[u], oy[u], ob[u]);
+  float4 acc[2][4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int g = g0 + j;
+    const float4 bj = g < cout4 ? __ldg(reinterpret_cast<const float4 *>(bias) + g) : make_float4(0, 0, 0, 0);
+    acc[0][j] = bj, acc[1][j] = bj;
+  }
+  for (int ky = 0; ky < k; ky++) {
+    for (int kx = 0; kx < k; kx++) {
+      const T *px[2];
+      bool ok[2];
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int iy = oy[u] * stride + ky - pad, ix = ox[u] * stride + kx - pad;
+        ok[u] = u < npx && iy >= 0 && iy < H && ix >= 0 && ix < W;
+        px[u] = src + (((long)ob[u] * H + (ok[u] ? iy : 0)) * W + (ok[u] ? ix : 0)) * Cin;
+      }
+      const float4 *wk = wsm + (ky * k + kx) * Cin * 4;
+      for (int c4 = 0; c4 < cin4; c4++) {
+        float xs[2][4];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          const float4 x = ok[u] ? Io<T>::load4(px[u] + c4 * 4) : make_float4(0, 0, 0, 0);
+          xs[u][0] = x.x, xs[u][1] = x.y, xs[u][2] = x.z, xs[u][3] = x.w;
+        }
+#pragma unroll
+        for (int qq = 0; qq < 4; qq++) {
+          const float4 *wr = wk + (c4 * 4 + qq) * 4;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const float4 wv = wr[j];
+#pragma unroll
+            for (int u = 0; u < 2; u++)
+              if (ok[u]) acc[u][j] = f4fma(make_float4(xs[u][qq], xs[u][qq], xs[u][qq], xs[u][qq]), wv, acc[u][j]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    if (u >= npx) break;
+    T *o = dst + (pix0 + u) * Cout;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int g = g0 + j;
+      if (g < cout4) {
+        float4 v = acc[u][j];
+        v = make_float4(act_apply(act, v.x), act_apply(act, v.y), act_apply(act, v.z), act_apply(act, v.w));
+        Io<T>::store4(o + g * 4, v);
+      }
+    }
+  }
+}
+
 cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const float *wpk, const float *bias, int Cout,
                  int k, int stride, int act, void *dst, cudaStream_t st) {
   int pad = (k - 1) >> 1;
@@ -207,6 +288,15 @@ cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const flo
   long total = (long)n * OH * OW;
   if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total <= 0) return cudaSuccess;
+  const size_t wsm = (size_t)k * k * Cin * 4 * sizeof(float4);
+  if (wsm <= 32 * 1024) {
+    dim3 grid(blocks_for((total + 1) / 2, 128), (Cout / 4 + 3) / 4);
+    if (T == F32)
+      return launch_pdl(k_conv_sw<float>, grid, dim3(128), wsm, st, (const float *)src, n, H, W, Cin, wpk, bias, Cout,
+                        k, stride, act, OH, OW, (float *)dst);
+    return launch_pdl(k_conv_sw<__nv_bfloat16>, grid, dim3(128), wsm, st, (const __nv_bfloat16 *)src, n, H, W, Cin,
+                      wpk, bias, Cout, k, stride, act, OH, OW, (__nv_bfloat16 *)dst);
+  }
   dim3 grid(blocks_for(total, 128), (Cout / 4 + 3) / 4);
   if (T == F32)
     return launch_pdl(k_conv<float>, grid, dim3(128), 0, st, (const float *)src, n, H, W, Cin, wpk, bias, Cout, k,
@@ -492,53 +582,76 @@ cudaError_t head(int T, const void *src, long M, int C, const float *w, float bi
 // low: (n, lh, lw) with channel stride lc; guide luma either precomputed
 // (luma, 1 channel) or from linear colour (guide, gc channels).
 // Parameter list mirrored by kBilateralArgCount / kBilateralDstArg.
+//
+// One thread per 2x2 output quad: output (x, y) centres its 3x3 low-res taps
+// on (floor((x + 0.5) / 2), floor((y + 0.5) / 2)), which is the same low
+// pixel for x = 2i and 2i + 1, so the quad loads the nine disparities and
+// nine guide values once; each output pixel then runs the reference's
+// per-pixel arithmetic unchanged.
 __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh, int lw,
                             const float *__restrict__ luma, const float *__restrict__ guide, int gc,
                             BilateralParams p, float *__restrict__ dst, const float *__restrict__ history,
                             float *__restrict__ out_tex) {
   pdl_wait();
   pdl_trigger();
-  int S = lh * 2, SW = lw * 2;
-  long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  long total = (long)n * S * SW;
-  if (idx >= total) return;
-  int x, y, b;
-  unflatten3(idx, SW, S, x, y, b);
+  const int S = lh * 2, SW = lw * 2;
+  const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= (long)n * lh * lw) return;
+  int qi, qj, b;
+  unflatten3(q, lw, lh, qi, qj, b);
   auto luma_at = [&](int gx, int gy) -> float {
-    long g = ((long)b * S + gy) * SW + gx;
+    const long g = ((long)b * S + gy) * SW + gx;
     if (luma) return __ldg(luma + g);
     const float *c = guide + g * gc;
     return 0.2126f * __ldg(c) + 0.7152f * __ldg(c + 1) + 0.0722f * __ldg(c + 2);
   };
-  float here = luma_at(x, y);
-  float cx = (x + 0.5f) * 0.5f - 0.5f, cy = (y + 0.5f) * 0.5f - 0.5f;
-  int bx = (int)floorf(cx + 0.5f), by = (int)floorf(cy + 0.5f);
-  float inv = 1.0f / fmaxf(p.range_sigma, 1e-4f);
-  float weighted = 0.0f, total_w = 0.0f;
+  float disp[9], there[9];
+  int tqx[9], tqy[9];
 #pragma unroll
   for (int dy = -1; dy <= 1; dy++)
 #pragma unroll
     for (int dx = -1; dx <= 1; dx++) {
-      int qx = min(max(bx + dx, 0), lw - 1), qy = min(max(by + dy, 0), lh - 1);
-      float disp = __ldg(low + (((long)b * lh + qy) * lw + qx) * lc);
-      float there = luma_at(qx * 2, qy * 2);
-      float dxs = qx - cx, dys = qy - cy;
-      float spatial = expf(-(dxs * dxs + dys * dys) * 0.5f);
-      float dl = (here - there) * inv;
-      float wgt = spatial * expf(-dl * dl * 0.5f);
-      weighted = fmaf(disp, wgt, weighted);
+      const int k = (dy + 1) * 3 + dx + 1;
+      const int qx = min(max(qi + dx, 0), lw - 1), qy = min(max(qj + dy, 0), lh - 1);
+      tqx[k] = qx, tqy[k] = qy;
+      disp[k] = __ldg(low + (((long)b * lh + qy) * lw + qx) * lc);
+      there[k] = luma_at(qx * 2, qy * 2);
+    }
+  const float inv = 1.0f / fmaxf(p.range_sigma, 1e-4f);
+  float out[4];
+#pragma unroll
+  for (int sub = 0; sub < 4; sub++) {
+    const int x = 2 * qi + (sub & 1), y = 2 * qj + (sub >> 1);
+    const float here = luma_at(x, y);
+    const float cx = (x + 0.5f) * 0.5f - 0.5f, cy = (y + 0.5f) * 0.5f - 0.5f;
+    float weighted = 0.0f, total_w = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 9; k++) {
+      const float dxs = tqx[k] - cx, dys = tqy[k] - cy;
+      const float spatial = expf(-(dxs * dxs + dys * dys) * 0.5f);
+      const float dl = (here - there[k]) * inv;
+      const float wgt = spatial * expf(-dl * dl * 0.5f);
+      weighted = fmaf(disp[k], wgt, weighted);
       total_w += wgt;
     }
-  float up = weighted / fmaxf(total_w, 1e-6f);
-  float out = up;
-  if (out_tex) {
-    float4 prev = history ? reinterpret_cast<const float4 *>(history)[idx] : make_float4(0, 0, 0, 0);
-    float change = fabsf(up - prev.x);
-    float alpha = prev.w < 0.5f ? 1.0f : fminf(fmaxf(p.base_alpha + change * p.sensitivity, p.base_alpha), 1.0f);
-    out = prev.x + (up - prev.x) * alpha;
-    reinterpret_cast<float4 *>(out_tex)[idx] = make_float4(out, up, change, 1.0f);
+    const float up = weighted / fmaxf(total_w, 1e-6f);
+    float o = up;
+    const long idx = ((long)b * S + y) * SW + x;
+    if (out_tex) {
+      const float4 prev = history ? reinterpret_cast<const float4 *>(history)[idx] : make_float4(0, 0, 0, 0);
+      const float change = fabsf(up - prev.x);
+      const float alpha =
+          prev.w < 0.5f ? 1.0f : fminf(fmaxf(p.base_alpha + change * p.sensitivity, p.base_alpha), 1.0f);
+      o = prev.x + (up - prev.x) * alpha;
+      reinterpret_cast<float4 *>(out_tex)[idx] = make_float4(o, up, change, 1.0f);
+    }
+    out[sub] = o;
   }
-  if (dst) dst[idx] = out;
+  if (dst) {  // scalar stores: callers' output pointers need only 4-byte alignment
+    const long row0 = ((long)b * S + 2 * qj) * SW + 2 * qi;
+    dst[row0] = out[0], dst[row0 + 1] = out[1];
+    dst[row0 + SW] = out[2], dst[row0 + SW + 1] = out[3];
+  }
 }
 
 cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *luma, const BilateralParams &p,
@@ -546,7 +659,7 @@ cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *lum
   long total = (long)n * lh * lw * 4;
   if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
-  return launch_pdl(k_bilateral, dim3(blocks_for(total, 256)), dim3(256), 0, st, low1, 1, n, lh, lw, luma,
+  return launch_pdl(k_bilateral, dim3(blocks_for(total / 4, 256)), dim3(256), 0, st, low1, 1, n, lh, lw, luma,
                     (const float *)nullptr, 0, p, dst, history, out_tex);
 }
 
@@ -556,8 +669,8 @@ cudaError_t bilateral_strided(const float *low, int lh, int lw, int low_c, const
   if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
   BilateralParams p{range_sigma, 0.35f, 3.0f};
-  k_bilateral<<<blocks_for(total, 256), 256, 0, st>>>(low, low_c, 1, lh, lw, nullptr, guide, guide_c, p, dst,
-                                                      nullptr, nullptr);
+  k_bilateral<<<blocks_for(total / 4, 256), 256, 0, st>>>(low, low_c, 1, lh, lw, nullptr, guide, guide_c, p, dst,
+                                                          nullptr, nullptr);
   return cudaGetLastError();
 }
 
