@@ -219,6 +219,10 @@ struct EpiArgs {
   void *dst;           // [M][N]
   int N, act, OH, OW;
   int n_tile;
+  // lateral: the tile's upsampled coarse term in shared memory, tile row r and
+  // output column n at cs[r * cs_ld + n - cs_n0]; null: computed from `coarse`
+  const float *cs;
+  int cs_ld, cs_n0;
 };
 
 // Accumulator-independent inputs of one 16-column block for the 4 rows a
@@ -231,6 +235,7 @@ struct EpiBlockIn {
 // Per-row pixel data of the rows a lane stores (fixed for a tile).
 struct EpiRows {
   long m[4];  // output pixel, -1 for a padding row
+  int r[4];   // tile row
 };
 
 template <typename T, int MODE>
@@ -244,40 +249,38 @@ __device__ __forceinline__ EpiBlockIn epi_block_in(const EpiArgs &a, const EpiRo
     in.x[i] = (col_ok && mm >= 0 && res) ? ld4(res + mm * a.N + n) : z;
   }
   if (MODE == 2) {
-    const T *coarse = reinterpret_cast<const T *>(a.coarse);
+    // the bilinear 2x upsample of the coarse map comes before the residual, as
+    // in the reference: from shared memory when it was computed ahead (a.cs),
+    // else from its four taps here
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const long mm = rows.m[i];
-      if (!col_ok || mm < 0) continue;
-      // refUpsample2 taps (reference.ts:161-193): (i + 0.5) / 2 - 0.5, both
-      // taps from the unclamped floor, clamped independently
-      // pixel indices stay below 2^31 (frames x OH x OW of one launch), so the
-      // decomposition uses 32-bit division
-      const uint32_t um = (uint32_t)mm, uow = (uint32_t)a.OW, uoh = (uint32_t)a.OH;
-      const uint32_t t = um / uow;
-      const int x = (int)(um - t * uow);
-      const uint32_t bb = t / uoh;
-      const int y = (int)(t - bb * uoh), b = (int)bb;
-      const int CH = a.OH >> 1, CW = a.OW >> 1;
-      const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
-      const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
-      const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
-      const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
-      const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
-      const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
-      const float4 c00 = ld4(coarse + (rr0 + x0) * a.N + n), c01 = ld4(coarse + (rr0 + x1) * a.N + n);
-      const float4 c10 = ld4(coarse + (rr1 + x0) * a.N + n), c11 = ld4(coarse + (rr1 + x1) * a.N + n);
-      // the coarse term is added before the residual, as in the reference
+      if (!col_ok || rows.m[i] < 0) continue;
       float4 c;
-      c.x = c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
-      c.y = c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
-      c.z = c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
-      c.w = c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
-      in.x[i] = make_float4(c.x, c.y, c.z, c.w);  // residual of a lateral is folded in below
-      if (res) {
-        const float4 q = ld4(res + mm * a.N + n);
-        in.x[i] = make_float4(c.x + q.x, c.y + q.y, c.z + q.z, c.w + q.w);
+      if (a.cs) {
+        c = *reinterpret_cast<const float4 *>(a.cs + rows.r[i] * a.cs_ld + (n - a.cs_n0));
+      } else {
+        const T *coarse = reinterpret_cast<const T *>(a.coarse);
+        const long mm = rows.m[i];
+        const uint32_t um = (uint32_t)mm, uow = (uint32_t)a.OW, uoh = (uint32_t)a.OH;
+        const uint32_t t = um / uow;
+        const int x = (int)(um - t * uow);
+        const uint32_t bb = t / uoh;
+        const int y = (int)(t - bb * uoh), b = (int)bb;
+        const int CH = a.OH >> 1, CW = a.OW >> 1;
+        const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
+        const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
+        const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
+        const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
+        const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
+        const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
+        const float4 c00 = ld4(coarse + (rr0 + x0) * a.N + n), c01 = ld4(coarse + (rr0 + x1) * a.N + n);
+        const float4 c10 = ld4(coarse + (rr1 + x0) * a.N + n), c11 = ld4(coarse + (rr1 + x1) * a.N + n);
+        c.x = c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
+        c.y = c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
+        c.z = c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
+        c.w = c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
       }
+      in.x[i] = res ? make_float4(c.x + in.x[i].x, c.y + in.x[i].y, c.z + in.x[i].z, c.w + in.x[i].w) : c;
     }
   }
   return in;
@@ -363,7 +366,7 @@ __device__ __forceinline__ bool epilogue_body(const EpiArgs &a, uint32_t tacc_la
     epi_block_stage(width, v, blk);
     if (cb1 < ncols) epi_block_ld(tacc_lane + (uint32_t)(col0 + cb1), min(kEpiCols, ncols - cb1), v);
     epi_block_store<T, ACT>(a, rows, n, col_ok, cur, blk);
-    if (cb1 < ncols) cur = epi_block_in<T, MODE>(a, rows, n1, ok1);
+    if (cb1 < ncols) cur = epi_block_in<T, MODE>(a, rows, n1, ok1);  // residual / coarse of the next block
   }
   return true;
 }
@@ -480,7 +483,7 @@ __device__ __forceinline__ bool epilogue_rows(const EpiArgs &a, uint32_t tacc_la
   const int rsub = (threadIdx.x & 31) >> 2;
   EpiRows rows;
 #pragma unroll
-  for (int i = 0; i < 4; i++) rows.m[i] = pix(lane_base + i * 8 + rsub);
+  for (int i = 0; i < 4; i++) rows.r[i] = lane_base + i * 8 + rsub, rows.m[i] = pix(rows.r[i]);
   switch (a.act) {
     case 1: return epilogue_body<T, MODE, 1>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
     case 2: return epilogue_body<T, MODE, 2>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);

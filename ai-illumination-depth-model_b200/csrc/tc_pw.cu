@@ -45,7 +45,49 @@ struct Params {
   long M;
   int n_tiles, m_tiles, slabs, stages;
   uint32_t acc_stride, tmem_cols, b_bytes, bias_bytes;
+  int cs_ld;           // lateral: row stride (floats) of the coarse ring's tiles
+  int cs_stages;       // lateral: coarse ring depth (0: the epilogue gathers the taps itself)
+  uint32_t cs_bytes;   // cs_stages * 128 * cs_ld * 4
 };
+
+// Lateral: the bilinear 2x upsample (refUpsample2, reference.ts:161-193:
+// source coordinate (i + 0.5) / 2 - 0.5, both taps from the unclamped floor,
+// clamped independently) of the coarse map for tile row `r` (pixel m0 + r),
+// columns [n0, n0 + n_tile) of N, into row r of `cs`.
+template <typename T>
+__device__ __forceinline__ void coarse_row(const EpiArgs &a, long M, long m0, int r, int n0, int n_tile, float *cs,
+                                           int cs_ld) {
+  const long m = m0 + r;
+  if (m >= M) return;
+  const T *coarse = reinterpret_cast<const T *>(a.coarse);
+  const uint32_t um = (uint32_t)m, uow = (uint32_t)a.OW, uoh = (uint32_t)a.OH;
+  const uint32_t t = um / uow;
+  const int x = (int)(um - t * uow);
+  const uint32_t bb = t / uoh;
+  const int y = (int)(t - bb * uoh), b = (int)bb;
+  const int CH = a.OH >> 1, CW = a.OW >> 1;
+  const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
+  const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
+  const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
+  const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
+  const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
+  const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
+  const T *p00 = coarse + (rr0 + x0) * a.N, *p01 = coarse + (rr0 + x1) * a.N;
+  const T *p10 = coarse + (rr1 + x0) * a.N, *p11 = coarse + (rr1 + x1) * a.N;
+  float *row = cs + (size_t)r * cs_ld;
+  const int ncol = min(n_tile, a.N - n0);
+#pragma unroll 4
+  for (int c = 0; c < ncol; c += 4) {
+    const int n = n0 + c;
+    const float4 c00 = ld4(p00 + n), c01 = ld4(p01 + n), c10 = ld4(p10 + n), c11 = ld4(p11 + n);
+    float4 o;
+    o.x = c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
+    o.y = c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
+    o.z = c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
+    o.w = c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
+    *reinterpret_cast<float4 *>(row + c) = o;
+  }
+}
 
 // MODE 0 pointwise, 2 lateral.
 template <typename T, int MODE>
@@ -61,12 +103,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
   const int S = p.stages;
   float *epi_smem = reinterpret_cast<float *>(base + S * stage_bytes);
   float *bias_smem = epi_smem + kEpiSmem / 4;
-  uint64_t *full = reinterpret_cast<uint64_t *>(base + S * stage_bytes + kEpiSmem + p.bias_bytes);
+  float *cs_smem = bias_smem + p.bias_bytes / 4;  // lateral coarse ring: 2 x [128][cs_ld]
+  uint64_t *full = reinterpret_cast<uint64_t *>(base + S * stage_bytes + kEpiSmem + p.bias_bytes + p.cs_bytes);
   uint64_t *lo_rdy = full + S;
   uint64_t *empty = lo_rdy + S;
   uint64_t *acc_full = empty + S;
   uint64_t *acc_empty = acc_full + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint64_t *c_full = acc_empty + 2;
+  uint64_t *c_empty = c_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(c_empty + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tile = p.epi.n_tile;
@@ -79,6 +124,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     for (int a = 0; a < 2; a++) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], kEpiWarps);
+      mbar_init(&c_full[a], kNumConv);
+      mbar_init(&c_empty[a], kEpiWarps);
     }
     fence_barrier_init();
   }
@@ -146,12 +193,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       }
     }
   } else if (warp < kEpiWarp0) {
-    // ------------------------------------------------------------ TF32 split
-    if (kF32) {
-      const int ct = tid - kConvWarp0 * 32;
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+    // ------------------------------------------ TF32 split, lateral coarse term
+    const int ct = tid - kConvWarp0 * 32;
+    int stage = 0, cst = 0;
+    uint32_t phase = 0, cph = 0;
+    const bool ring = MODE == 2 && p.cs_stages > 0;
+    if (ring) pdl_wait();  // the coarse map is an earlier kernel's output
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      if (kF32) {
         for (int s = 0; s < p.slabs; s++) {
           if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase))) {
             ok = false;
@@ -171,6 +220,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
           if (lane == 0) mbar_arrive(&lo_rdy[stage]);
           if (++stage == S) stage = 0, phase ^= 1u;
         }
+        if (!ok) break;
+      }
+      if (ring) {
+        // one tile row per thread, ahead of the epilogue
+        if (!__all_sync(0xffffffffu, mbar_wait(&c_empty[cst], cph ^ 1u))) {
+          ok = false;
+          break;
+        }
+        const int mt = t / p.n_tiles, nt = t % p.n_tiles;
+        coarse_row<T>(p.epi, p.M, (long)mt * kTileM, ct, nt * n_tile, n_tile, cs_smem + cst * kTileM * p.cs_ld,
+                      p.cs_ld);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c_full[cst]);
+        if (++cst == p.cs_stages) cst = 0, cph ^= 1u;
       }
     }
   } else {
@@ -179,10 +242,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     const int lane_base = (warp & 3) * 32;
     const int half = n_tile / 2;
     float *blk = epi_smem + e * 32 * kEpiStride;
-    int acc = 0;
-    uint32_t acc_phase = 0;
+    int acc = 0, cst = 0;
+    uint32_t acc_phase = 0, cph = 0;
     EpiArgs ea = p.epi;
     ea.bias = bias_smem;
+    ea.cs = nullptr;
+    ea.cs_ld = p.cs_ld;
     pdl_wait();  // residual / coarse reads and the stores follow the previous kernel
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
@@ -190,6 +255,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       const long M = p.M;
       uint64_t *full = &acc_full[acc];
       const uint32_t ph = acc_phase;
+      if (MODE == 2 && p.cs_stages > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&c_full[cst], cph))) {
+          ok = false;
+          break;
+        }
+        ea.cs = cs_smem + cst * kTileM * p.cs_ld;
+        ea.cs_n0 = nt * n_tile;
+      }
       if (!epilogue_rows<T, MODE>(ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base,
                                   (e >> 2) * half, half, nt * n_tile, blk,
                                   [m0, M](int r) -> long { return m0 + r < M ? m0 + r : -1; },
@@ -205,6 +278,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) acc = 0, acc_phase ^= 1u;
+      if (MODE == 2 && p.cs_stages > 0) {
+        if (lane == 0) mbar_arrive(&c_empty[cst]);
+        if (++cst == p.cs_stages) cst = 0, cph ^= 1u;
+      }
     }
   }
 
@@ -299,12 +376,27 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.b_bytes = (uint32_t)(terms * plan.n_tile * 128);
   const size_t stage = terms * tcx::kAImage + p.b_bytes;
   p.bias_bytes = (uint32_t)(((size_t)op.N * 4 + 15) / 16 * 16);
-  const size_t fixed = 1024 + tcx::kEpiSmem + p.bias_bytes + 8 * (3 * 8 + 4) + 16;
+  // lateral coarse ring: row stride = 16 mod 32 floats, so the two rows a
+  // quarter-warp reads fall in different bank halves
+  p.cs_ld = plan.n_tile + (plan.n_tile % 32 == 0 ? 16 : 0);
+  // deepest coarse ring (2, 1 or none) that leaves at least 3 (else 2) A/B stages
+  const size_t cs_stage = (size_t)tcx::kTileM * p.cs_ld * 4;
+  const size_t fixed0 = 1024 + tcx::kEpiSmem + p.bias_bytes + 8 * (3 * 8 + 8) + 16;
+  p.cs_stages = 0;
+  if (op.mode == 2)
+    for (int want_ab = 3; want_ab >= 2 && !p.cs_stages; want_ab--)
+      for (int cs = 2; cs >= 1; cs--)
+        if (fixed0 + cs * cs_stage + want_ab * stage <= kSmemBudget) {
+          p.cs_stages = cs;
+          break;
+        }
+  p.cs_bytes = (uint32_t)(p.cs_stages * cs_stage);
+  const size_t fixed = fixed0 + p.cs_bytes;
   int stages = (int)((kSmemBudget - fixed) / stage);
   if (stages > 6) stages = 6;
   if (stages < 2) return cudaErrorInvalidValue;
   p.stages = stages;
-  const size_t smem = stages * stage + 1024 + tcx::kEpiSmem + p.bias_bytes + 8 * (3 * stages + 4) + 16;
+  const size_t smem = stages * stage + 1024 + tcx::kEpiSmem + p.bias_bytes + p.cs_bytes + 8 * (3 * stages + 8) + 16;
   if (T == F32) return op.mode == 0 ? launch<float, 0>(map, p, smem, st) : launch<float, 2>(map, p, smem, st);
   return op.mode == 0 ? launch<__nv_bfloat16, 0>(map, p, smem, st) : launch<__nv_bfloat16, 2>(map, p, smem, st);
 }
