@@ -96,6 +96,11 @@ __device__ __forceinline__ void unflatten3(long idx, int W, int H, int &x, int &
 }
 constexpr long kMaxIndex = 0x7fffffffL;
 
+bool &pdl_enabled() {
+  static thread_local bool on = false;
+  return on;
+}
+
 // ---------------------------------------------------------------------------
 // preprocess (src/model/kernels/io.ts:64-118 semantics, refPreprocess)
 // ---------------------------------------------------------------------------

@@ -21,6 +21,7 @@
 #include "host.h"
 #include "illumina.h"
 #include "kernels.h"
+#include "pdl.cuh"
 
 using namespace illumina;
 
@@ -56,6 +57,8 @@ constexpr size_t kSplitKBytes = 16u << 20;
 constexpr int kSplitKItems = 8192;
 constexpr size_t kSplitKOpBytes = 8u << 20;
 constexpr int kSplitKOpItems = 4096;
+// Largest batch whose forward uses programmatic dependent launch.
+constexpr int kPdlMaxBatch = 16;
 
 void cuda_check(cudaError_t e, const char *what) {
   if (e != cudaSuccess)
@@ -221,6 +224,13 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
   const int S = a.input_size;
   int launches = 0;
   cudaStream_t st = m.stream;
+  // programmatic dependent launch for small batches (kernels overlap their
+  // prologue with the predecessor's tail); restored when this forward is queued
+  struct PdlScope {
+    bool saved;
+    explicit PdlScope(bool on) : saved(gpu::pdl_enabled()) { gpu::pdl_enabled() = on; }
+    ~PdlScope() { gpu::pdl_enabled() = saved; }
+  } pdl(n <= kPdlMaxBatch);
   for (size_t i = 0; i < a.ops.size(); i++) {
     const Op &op = a.ops[i];
     if (marks) cuda_check(cudaEventRecord((*marks)[i], st), "profile event");

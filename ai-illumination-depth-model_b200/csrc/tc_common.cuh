@@ -64,6 +64,24 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
+// TMA tensor stores (shared -> global, bulk-group completion) and their waits.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Every committed store group has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed store group has completed (writes done).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
@@ -459,6 +477,127 @@ __device__ __noinline__ void epilogue_reduce(const EpiArgs a, const float *part,
     case 2: reduce_units<T, 2>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
     case 3: reduce_units<T, 3>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
     default: reduce_units<T, 0>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
+  }
+}
+
+__device__ __forceinline__ void bar_named(int id, int n);
+
+// TMA-store epilogue. The tile's output columns go out in 16-column slices:
+// each lane owns accumulator row `row` (its TMEM lane), adds bias and
+// residual, applies the activation and writes its 16 values into a slice
+// buffer in the layout of the output tensor map's box (rows of 16 columns,
+// SWIZZLE_64B for fp32, SWIZZLE_32B for bf16); once the four warps of the
+// group have written a pair of slices, one elected thread issues
+// `store(buffer, c0)` for each (a TMA store of columns [c0, c0 + 16) of the
+// tile) and commits them; before the pair of buffers is rewritten those
+// stores have finished reading it (`slice` counts pairs across tiles). Rows with
+// m < 0 (padding) are not written (the box does not cover them, or TMA clips
+// them at the tensor edge).
+constexpr int kSliceCols = 16;
+constexpr uint32_t kSliceBytes = kTileM * kSliceCols * 4;  // one fp32 slice buffer
+
+template <typename T>
+__device__ __forceinline__ void slice_put(uint8_t *buf, int row, const float (&o)[kSliceCols]);
+template <>
+__device__ __forceinline__ void slice_put<float>(uint8_t *buf, int row, const float (&o)[kSliceCols]) {
+#pragma unroll
+  for (int c = 0; c < 4; c++)
+    *reinterpret_cast<float4 *>(buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4)) =
+        make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+}
+template <>
+__device__ __forceinline__ void slice_put<__nv_bfloat16>(uint8_t *buf, int row, const float (&o)[kSliceCols]) {
+#pragma unroll
+  for (int c = 0; c < 2; c++) {
+    uint4 u;
+    uint32_t *pu = &u.x;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * c + 2 * j], o[8 * c + 2 * j + 1]);
+      pu[j] = *reinterpret_cast<uint32_t *>(&b2);
+    }
+    *reinterpret_cast<uint4 *>(buf + row * 32 + ((c ^ ((row >> 2) & 1)) << 4)) = u;
+  }
+}
+// Residual of one row's 16 slice columns (zero where absent or past N).
+template <typename T>
+__device__ __forceinline__ void slice_res(const EpiArgs &a, long m, int n, float (&r)[kSliceCols]) {
+  const T *res = reinterpret_cast<const T *>(a.res);
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    float4 q = make_float4(0, 0, 0, 0);
+    if (res && m >= 0 && n + 4 * c < a.N) q = ld4(res + m * a.N + n + 4 * c);
+    r[4 * c] = q.x, r[4 * c + 1] = q.y, r[4 * c + 2] = q.z, r[4 * c + 3] = q.w;
+  }
+}
+
+template <typename T, int ACT, typename ReadyFn, typename ReleaseFn, typename StoreFn>
+__device__ __forceinline__ bool epilogue_tma_body(const EpiArgs &a, uint32_t tacc_lane, int row, int ncols, int n_base,
+                                                  long m, uint8_t *bufs, uint32_t &slice, bool elected, int bar_id,
+                                                  int bar_n, ReadyFn ready, ReleaseFn release, StoreFn store) {
+  float rv[kSliceCols];
+  slice_res<T>(a, m, n_base, rv);
+  if (!ready()) return false;
+  // slices go out in pairs (32 columns): one barrier pair and two stores per
+  // pair, into one pair of buffers
+  for (int cb = 0; cb < ncols; cb += 2 * kSliceCols) {
+    uint8_t *buf = bufs;
+    if (elected) bulk_wait_read0();  // the previous pair's stores have finished reading the buffers
+    bar_named(bar_id, bar_n);
+    const int pair = min(2, (ncols - cb) / kSliceCols);
+    for (int h = 0; h < pair; h++) {
+      const int c = cb + h * kSliceCols;
+      uint32_t v[kSliceCols];
+      tmem_ld8_nowait(tacc_lane + (uint32_t)c, v);
+      tmem_ld8_nowait(tacc_lane + (uint32_t)c + 8, v + 8);
+      tmem_wait_ld();
+      if (c + kSliceCols >= ncols) release();  // the accumulator is free once its last columns are read
+      float o[kSliceCols];
+      const int n = n_base + c;
+#pragma unroll
+      for (int j = 0; j < kSliceCols; j += 4) {
+        float4 bias = make_float4(0, 0, 0, 0);
+        if (n + j < a.N) bias = *reinterpret_cast<const float4 *>(a.bias + n + j);
+        o[j] = __uint_as_float(v[j]) + bias.x + rv[j];
+        o[j + 1] = __uint_as_float(v[j + 1]) + bias.y + rv[j + 1];
+        o[j + 2] = __uint_as_float(v[j + 2]) + bias.z + rv[j + 2];
+        o[j + 3] = __uint_as_float(v[j + 3]) + bias.w + rv[j + 3];
+      }
+      if (c + kSliceCols < ncols) slice_res<T>(a, m, n + kSliceCols, rv);  // next slice's residual in flight
+#pragma unroll
+      for (int j = 0; j < kSliceCols; j++) o[j] = act_c<ACT>(o[j]);
+      if (m >= 0) slice_put<T>(buf + h * kSliceBytes, row, o);
+    }
+    fence_async_smem();
+    bar_named(bar_id, bar_n);
+    if (elected) {
+      for (int h = 0; h < pair; h++) store(smem_u32(buf + h * kSliceBytes), cb + h * kSliceCols);
+      bulk_commit();
+    }
+    slice++;
+  }
+  return true;
+}
+
+// `row`: the lane's accumulator row (its TMEM lane); `m`: that row's output
+// pixel or -1.
+template <typename T, typename ReadyFn, typename ReleaseFn, typename StoreFn>
+__device__ __forceinline__ bool epilogue_tma(const EpiArgs &a, uint32_t tacc_lane, int row, int ncols, int n_base,
+                                             long m, uint8_t *bufs, uint32_t &slice, bool elected, int bar_id,
+                                             int bar_n, ReadyFn ready, ReleaseFn release, StoreFn store) {
+  switch (a.act) {
+    case 1:
+      return epilogue_tma_body<T, 1>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
+                                     release, store);
+    case 2:
+      return epilogue_tma_body<T, 2>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
+                                     release, store);
+    case 3:
+      return epilogue_tma_body<T, 3>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
+                                     release, store);
+    default:
+      return epilogue_tma_body<T, 0>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
+                                     release, store);
   }
 }
 

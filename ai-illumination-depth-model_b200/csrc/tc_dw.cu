@@ -71,14 +71,14 @@ __global__ void k_pack_dw_slabs(const float *dw_w, const float *dw_b, int C, int
 
 
 // Instantiated in tc_dw_{f32,bf16}{,_split}.cu.
-extern template cudaError_t launch_all<float, false>(int, int, int, const CUtensorMap &, const Params &, size_t,
-                                                     cudaStream_t);
-extern template cudaError_t launch_all<float, true>(int, int, int, const CUtensorMap &, const Params &, size_t,
-                                                    cudaStream_t);
-extern template cudaError_t launch_all<__nv_bfloat16, false>(int, int, int, const CUtensorMap &, const Params &,
-                                                             size_t, cudaStream_t);
-extern template cudaError_t launch_all<__nv_bfloat16, true>(int, int, int, const CUtensorMap &, const Params &,
-                                                            size_t, cudaStream_t);
+extern template cudaError_t launch_all<float, false>(int, int, int, const CUtensorMap &, const CUtensorMap &,
+                                               const Params &, size_t, cudaStream_t);
+extern template cudaError_t launch_all<float, true>(int, int, int, const CUtensorMap &, const CUtensorMap &,
+                                               const Params &, size_t, cudaStream_t);
+extern template cudaError_t launch_all<__nv_bfloat16, false>(int, int, int, const CUtensorMap &, const CUtensorMap &,
+                                               const Params &, size_t, cudaStream_t);
+extern template cudaError_t launch_all<__nv_bfloat16, true>(int, int, int, const CUtensorMap &, const CUtensorMap &,
+                                               const Params &, size_t, cudaStream_t);
 
 }  // namespace tcd
 
@@ -248,6 +248,18 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // output: 16-column slices of a th x tw patch, rows of 64 B (fp32) or 32 B
+  // (bf16) in the epilogue's swizzled slice buffers
+  CUtensorMap map_out;
+  cuuint64_t odims[4] = {(cuuint64_t)op.N, (cuuint64_t)op.OW, (cuuint64_t)op.OH, (cuuint64_t)op.n};
+  cuuint64_t ostrides[3] = {(cuuint64_t)op.N * elt, (cuuint64_t)op.OW * op.N * elt,
+                            (cuuint64_t)op.OH * op.OW * op.N * elt};
+  cuuint32_t obox[4] = {(cuuint32_t)tcx::kSliceCols, (cuuint32_t)tl.tw, (cuuint32_t)tl.th, 1};
+  r = encode(&map_out, T == F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, op.dst, odims,
+             ostrides, obox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             T == F32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
 
   const int terms = T == F32 ? 2 : 1;
   tcd::Params p;
@@ -275,10 +287,10 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.bias_bytes = (uint32_t)align_to((size_t)op.N * 4, 16);
   const bool split = tl.ksplit > 1;
   if (T == F32)
-    return split ? tcd::launch_all<float, true>(op.ks, op.stride, tl.P, map, p, tl.smem, st)
-                 : tcd::launch_all<float, false>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
-  return split ? tcd::launch_all<__nv_bfloat16, true>(op.ks, op.stride, tl.P, map, p, tl.smem, st)
-               : tcd::launch_all<__nv_bfloat16, false>(op.ks, op.stride, tl.P, map, p, tl.smem, st);
+    return split ? tcd::launch_all<float, true>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st)
+                 : tcd::launch_all<float, false>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st);
+  return split ? tcd::launch_all<__nv_bfloat16, true>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st)
+               : tcd::launch_all<__nv_bfloat16, false>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st);
 }
 
 }  // namespace gpu

@@ -5,8 +5,8 @@
 namespace illumina {
 namespace gpu {
 namespace tcd {
-template cudaError_t launch_all<__nv_bfloat16, false>(int, int, int, const CUtensorMap &, const Params &, size_t,
-                                                         cudaStream_t);
+template cudaError_t launch_all<__nv_bfloat16, false>(int, int, int, const CUtensorMap &, const CUtensorMap &, const Params &,
+                                        size_t, cudaStream_t);
 }  // namespace tcd
 }  // namespace gpu
 }  // namespace illumina

@@ -60,7 +60,9 @@ using namespace tcx;
 constexpr int kMmaWarp = 1, kXfWarp0 = 2, kGroupWarps = 4, kMaxGroups = 2, kEpiWarp0 = 10, kEpiW = 4,
               kBWarp = 14;
 constexpr int kThreads = 32 * (kBWarp + 1);
-constexpr uint32_t kEpiBytes = kEpiW * 32 * kEpiStride * 4;
+// one pair of TMA-store slice buffers, or the transposed-store blocks of wide tiles
+constexpr uint32_t kEpiBytes = 2 * kSliceBytes > kEpiW * 32 * kEpiStride * 4 ? 2 * kSliceBytes
+                                                                             : kEpiW * 32 * kEpiStride * 4;
 
 struct Params {
   const uint8_t *wimg;   // pointwise images [n tile][slab], b_bytes each
@@ -190,7 +192,8 @@ __device__ __forceinline__ void depthwise_dispatch(const Params &p, const Item &
 // SPLIT: the launch splits K (p.ksplit > 1); a separate instantiation keeps
 // the split-K epilogue out of the common kernel's code and registers.
 template <typename T, int KS, int S, int P, bool SPLIT>
-__global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ CUtensorMap tmap, const Params p) {
+__global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ CUtensorMap tmap,
+                                                       const __grid_constant__ CUtensorMap tmap_out, const Params p) {
   constexpr bool kF32 = sizeof(T) == 4;
   constexpr int kTerms = kF32 ? 2 : 1;
   constexpr int kSlabC = 128 / (int)sizeof(T);
@@ -373,7 +376,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     // ------------------------------------------------------- epilogue
     const int e = warp - kEpiWarp0;
     const int lane_base = (warp & 3) * 32;
-    float *blk = epi_smem + e * 32 * kEpiStride;
     int acc = 0;
     uint32_t acc_phase = 0;
     const int tw = p.tw, th = p.th, OH = p.epi.OH, OW = p.epi.OW;
@@ -388,7 +390,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         return ((long)it.b * OH + y) * OW + x;
       };
     };
-    if constexpr (!SPLIT) {
+    if (!SPLIT && n_tile > 2 * kSliceCols) {
+      // wide tiles: transposed stores straight from the epilogue warps
+      float *blk = epi_smem + e * 32 * kEpiStride;
       for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
         const Item it = decode<SPLIT>(p, t);
         uint64_t *full = &acc_full[acc];
@@ -407,6 +411,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
         if (++acc == 2) acc = 0, acc_phase ^= 1u;
       }
+    } else if (!SPLIT) {
+      // tiles of up to 32 columns: TMA-store epilogue, 16-column slices of the
+      // patch go out as 4-D boxes (tensor edges clipped by TMA); the four warps
+      // meet at named barrier 1.
+      uint8_t *bufs = reinterpret_cast<uint8_t *>(epi_smem);
+      const bool elected = warp == kEpiWarp0 && lane == 0;
+      uint32_t slice = 0;
+      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
+        const Item it = decode<SPLIT>(p, t);
+        uint64_t *full = &acc_full[acc];
+        const uint32_t ph = acc_phase;
+        uint64_t *empty_bar = &acc_empty[acc];
+        const int row = lane_base + lane;
+        const long m = pix_of(it)(row);
+        const int n0 = it.nt * n_tile;
+        if (!epilogue_tma<T>(
+                ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), row, n_tile, n0, m, bufs, slice,
+                elected, 1, kEpiW * 32,
+                [full, ph]() {
+                  const bool w = bar_and(1, kEpiW * 32, mbar_wait(full, ph));
+                  tc_fence_after();
+                  return w;
+                },
+                [empty_bar, lane]() {
+                  tc_fence_before();
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive(empty_bar);
+                },
+                [&tmap_out, it, n0](uint32_t src, int cb) { tma_store_4d(&tmap_out, src, n0 + cb, it.x0, it.y0, it.b); })) {
+          ok = false;
+          break;
+        }
+        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+      }
+      if (elected) bulk_wait_all();  // the output is written before the CTA leaves
     } else {
       // split-K: write this split's partial tile, release the accumulator; the
       // CTA that brings the item's last partial sums them and stores the item.
@@ -454,7 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
 constexpr size_t kSmemBudget = 227 * 1024;
 
 template <typename T, int KS, int S, int P, bool SPLIT>
-cudaError_t launch_dw(const CUtensorMap &map, const tcd::Params &p, size_t smem, cudaStream_t st) {
+cudaError_t launch_dw(const CUtensorMap &map, const CUtensorMap &map_out, const tcd::Params &p, size_t smem,
+                      cudaStream_t st) {
   auto kern = tcd::k_tc_dw<T, KS, S, P, SPLIT>;
   static unsigned long long granted = 0;
   int dev = 0;
@@ -465,27 +505,28 @@ cudaError_t launch_dw(const CUtensorMap &map, const tcd::Params &p, size_t smem,
     granted |= 1ull << dev;
   }
   const unsigned grid = (unsigned)(p.total < sm_count() ? p.total : sm_count());
-  return launch_pdl(kern, dim3(grid), dim3(tcd::kThreads), smem, st, map, p);
+  return launch_pdl(kern, dim3(grid), dim3(tcd::kThreads), smem, st, map, map_out, p);
 }
 
 template <typename T, int KS, int S, bool SPLIT>
-cudaError_t launch_p(int P, const CUtensorMap &map, const tcd::Params &p, size_t smem, cudaStream_t st) {
+cudaError_t launch_p(int P, const CUtensorMap &map, const CUtensorMap &map_out, const tcd::Params &p, size_t smem,
+                     cudaStream_t st) {
   switch (P) {
-    case 8: return launch_dw<T, KS, S, 8, SPLIT>(map, p, smem, st);
-    case 7: return launch_dw<T, KS, S, 7, SPLIT>(map, p, smem, st);
-    case 4: return launch_dw<T, KS, S, 4, SPLIT>(map, p, smem, st);
-    case 2: return launch_dw<T, KS, S, 2, SPLIT>(map, p, smem, st);
+    case 8: return launch_dw<T, KS, S, 8, SPLIT>(map, map_out, p, smem, st);
+    case 7: return launch_dw<T, KS, S, 7, SPLIT>(map, map_out, p, smem, st);
+    case 4: return launch_dw<T, KS, S, 4, SPLIT>(map, map_out, p, smem, st);
+    case 2: return launch_dw<T, KS, S, 2, SPLIT>(map, map_out, p, smem, st);
     default: return cudaErrorInvalidValue;
   }
 }
 // Launch of the instance for (KS, S, P); SPLIT must match p.ksplit > 1.
 template <typename T, bool SPLIT>
-cudaError_t launch_all(int KS, int S, int P, const CUtensorMap &map, const tcd::Params &p, size_t smem,
-                     cudaStream_t st) {
-  if (KS == 3 && S == 1) return launch_p<T, 3, 1, SPLIT>(P, map, p, smem, st);
-  if (KS == 3 && S == 2) return launch_p<T, 3, 2, SPLIT>(P, map, p, smem, st);
-  if (KS == 5 && S == 1) return launch_p<T, 5, 1, SPLIT>(P, map, p, smem, st);
-  if (KS == 5 && S == 2) return launch_p<T, 5, 2, SPLIT>(P, map, p, smem, st);
+cudaError_t launch_all(int KS, int S, int P, const CUtensorMap &map, const CUtensorMap &map_out, const tcd::Params &p,
+                       size_t smem, cudaStream_t st) {
+  if (KS == 3 && S == 1) return launch_p<T, 3, 1, SPLIT>(P, map, map_out, p, smem, st);
+  if (KS == 3 && S == 2) return launch_p<T, 3, 2, SPLIT>(P, map, map_out, p, smem, st);
+  if (KS == 5 && S == 1) return launch_p<T, 5, 1, SPLIT>(P, map, map_out, p, smem, st);
+  if (KS == 5 && S == 2) return launch_p<T, 5, 2, SPLIT>(P, map, map_out, p, smem, st);
   return cudaErrorInvalidValue;
 }
 
