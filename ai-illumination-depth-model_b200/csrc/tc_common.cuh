@@ -80,6 +80,8 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t sr
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Every committed store group has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// At most the most recent committed store group may still be reading.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // Every committed store group has completed (writes done).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar) {
@@ -598,6 +600,75 @@ __device__ __forceinline__ bool epilogue_tma(const EpiArgs &a, uint32_t tacc_lan
     default:
       return epilogue_tma_body<T, 0>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
                                      release, store);
+  }
+}
+
+// Per-warp TMA-store epilogue for tiles whose 32 rows per warp are 32
+// consecutive output pixels (pointwise / lateral): lane = accumulator row,
+// values go through a 32-row x 16-column swizzled slice (two per warp,
+// alternating) and lane 0 stores each as a 2-D box; no other warp is waited
+// for. `m`: the lane's output pixel or -1; `cs_row`: for laterals, the lane's
+// row of the upsampled coarse term in shared memory (columns relative to the
+// tile), else null.
+constexpr uint32_t kWarpSliceBytes = 32 * kSliceCols * 4;
+
+template <typename T, int ACT, typename ReadyFn, typename ReleaseFn, typename StoreFn>
+__device__ __forceinline__ bool warp_tma_body(const EpiArgs &a, uint32_t tacc_lane, int col0, int ncols, int n_base,
+                                              long m, const float *cs_row, uint8_t *wbuf, uint32_t &blocks,
+                                              ReadyFn ready, ReleaseFn release, StoreFn store) {
+  const int lane = threadIdx.x & 31;
+  float rv[kSliceCols];
+  slice_res<T>(a, m, n_base + col0, rv);
+  if (!ready()) return false;
+  for (int cb = 0; cb < ncols; cb += kSliceCols) {
+    uint32_t v[kSliceCols];
+    tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb), v);
+    tmem_ld8_nowait(tacc_lane + (uint32_t)(col0 + cb) + 8, v + 8);
+    tmem_wait_ld();
+    if (cb + kSliceCols >= ncols) release();
+    const int n = n_base + col0 + cb;
+    float o[kSliceCols];
+#pragma unroll
+    for (int j = 0; j < kSliceCols; j += 4) {
+      float4 bias = make_float4(0, 0, 0, 0), c = make_float4(0, 0, 0, 0);
+      if (n + j < a.N) {
+        bias = *reinterpret_cast<const float4 *>(a.bias + n + j);
+        if (cs_row) c = *reinterpret_cast<const float4 *>(cs_row + col0 + cb + j);
+      }
+      // acc + bias, then the coarse term (laterals), then the residual
+      o[j] = __uint_as_float(v[j]) + bias.x + c.x + rv[j];
+      o[j + 1] = __uint_as_float(v[j + 1]) + bias.y + c.y + rv[j + 1];
+      o[j + 2] = __uint_as_float(v[j + 2]) + bias.z + c.z + rv[j + 2];
+      o[j + 3] = __uint_as_float(v[j + 3]) + bias.w + c.w + rv[j + 3];
+    }
+    if (cb + kSliceCols < ncols) slice_res<T>(a, m, n + kSliceCols, rv);
+#pragma unroll
+    for (int j = 0; j < kSliceCols; j++) o[j] = act_c<ACT>(o[j]);
+    uint8_t *buf = wbuf + (blocks & 1) * kWarpSliceBytes;
+    if (lane == 0) bulk_wait_read1();  // this buffer's previous store has finished reading it
+    __syncwarp();
+    if (m >= 0) slice_put<T>(buf, lane, o);
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      store(smem_u32(buf), col0 + cb);
+      bulk_commit();
+    }
+    blocks++;
+  }
+  return true;
+}
+
+template <typename T, typename ReadyFn, typename ReleaseFn, typename StoreFn>
+__device__ __forceinline__ bool warp_tma_epilogue(const EpiArgs &a, uint32_t tacc_lane, int col0, int ncols, int n_base,
+                                                  long m, const float *cs_row, uint8_t *wbuf, uint32_t &blocks,
+                                                  ReadyFn ready, ReleaseFn release, StoreFn store) {
+  switch (a.act) {
+    case 1: return warp_tma_body<T, 1>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
+    case 2: return warp_tma_body<T, 2>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
+    case 3: return warp_tma_body<T, 3>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
+    default:
+      return warp_tma_body<T, 0>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
   }
 }
 

@@ -37,6 +37,9 @@ using namespace tcx;
 
 constexpr int kMmaWarp = 1, kConvWarp0 = 2, kNumConv = 4, kEpiWarp0 = 6;
 constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+// epilogue shared memory: two TMA-store slices per warp, or (laterals without
+// the coarse ring) the transposed-store blocks
+constexpr uint32_t kEpiPw = 2 * kEpiWarps * kWarpSliceBytes > kEpiSmem ? 2 * kEpiWarps * kWarpSliceBytes : kEpiSmem;
 
 struct Params {
   const uint8_t *wimg;  // [n tile][slab] images of b_bytes
@@ -91,7 +94,8 @@ __device__ __forceinline__ void coarse_row(const EpiArgs &a, long M, long m0, in
 
 // MODE 0 pointwise, 2 lateral.
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ CUtensorMap tmap_a, const Params p) {
+__global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ CUtensorMap tmap_a,
+                                                       const __grid_constant__ CUtensorMap tmap_out, const Params p) {
   constexpr bool kF32 = sizeof(T) == 4;
   constexpr int kTerms = kF32 ? 2 : 1;
   constexpr int kSlabC = 128 / (int)sizeof(T);
@@ -102,9 +106,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
   const uint32_t stage_bytes = kTerms * kAImage + p.b_bytes;
   const int S = p.stages;
   float *epi_smem = reinterpret_cast<float *>(base + S * stage_bytes);
-  float *bias_smem = epi_smem + kEpiSmem / 4;
+  float *bias_smem = epi_smem + kEpiPw / 4;
   float *cs_smem = bias_smem + p.bias_bytes / 4;  // lateral coarse ring: 2 x [128][cs_ld]
-  uint64_t *full = reinterpret_cast<uint64_t *>(base + S * stage_bytes + kEpiSmem + p.bias_bytes + p.cs_bytes);
+  uint64_t *full = reinterpret_cast<uint64_t *>(base + S * stage_bytes + kEpiPw + p.bias_bytes + p.cs_bytes);
   uint64_t *lo_rdy = full + S;
   uint64_t *empty = lo_rdy + S;
   uint64_t *acc_full = empty + S;
@@ -241,7 +245,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     const int e = warp - kEpiWarp0;
     const int lane_base = (warp & 3) * 32;
     const int half = n_tile / 2;
-    float *blk = epi_smem + e * 32 * kEpiStride;
     int acc = 0, cst = 0;
     uint32_t acc_phase = 0, cph = 0;
     EpiArgs ea = p.epi;
@@ -249,12 +252,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     ea.cs = nullptr;
     ea.cs_ld = p.cs_ld;
     pdl_wait();  // residual / coarse reads and the stores follow the previous kernel
+    // per-warp TMA stores of whole 16-column slices, unless a warp's column
+    // half is not a multiple of 16 (a slice would spill into the other half)
+    // or a lateral gathers its coarse taps itself
+    const bool tma_out = (MODE == 0 || p.cs_stages > 0) && half % kSliceCols == 0;
+    uint8_t *wbuf = reinterpret_cast<uint8_t *>(epi_smem) + e * 2 * kWarpSliceBytes;
+    float *blk = epi_smem + e * 32 * kEpiStride;
+    uint32_t blocks = 0;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
       const long m0 = (long)mt * kTileM;
       const long M = p.M;
       uint64_t *full = &acc_full[acc];
+      uint64_t *empty_bar = &acc_empty[acc];
       const uint32_t ph = acc_phase;
+      const uint32_t tacc = tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16);
+      const float *cs_row = nullptr;
       if (MODE == 2 && p.cs_stages > 0) {
         if (!__all_sync(0xffffffffu, mbar_wait(&c_full[cst], cph))) {
           ok = false;
@@ -262,27 +275,46 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
         }
         ea.cs = cs_smem + cst * kTileM * p.cs_ld;
         ea.cs_n0 = nt * n_tile;
+        cs_row = ea.cs + (lane_base + lane) * p.cs_ld;
       }
-      if (!epilogue_rows<T, MODE>(ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base,
-                                  (e >> 2) * half, half, nt * n_tile, blk,
-                                  [m0, M](int r) -> long { return m0 + r < M ? m0 + r : -1; },
-                                  [full, ph]() {
-                                    const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph));
-                                    tc_fence_after();
-                                    return w;
-                                  })) {
-        ok = false;
-        break;
+      auto ready = [full, ph]() {
+        const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph));
+        tc_fence_after();
+        return w;
+      };
+      if (tma_out) {
+        const long mrow = m0 + lane_base + lane < M ? m0 + lane_base + lane : -1;
+        const int n_base = nt * n_tile;
+        if (!warp_tma_epilogue<T>(
+                ea, tacc, (e >> 2) * half, half, n_base, mrow, cs_row, wbuf, blocks, ready,
+                [empty_bar, lane]() {
+                  tc_fence_before();
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive(empty_bar);
+                },
+                [&tmap_out, n_base, m0, lane_base](uint32_t src, int c) {
+                  tma_store_2d(&tmap_out, src, n_base + c, (int)(m0 + lane_base));
+                })) {
+          ok = false;
+          break;
+        }
+      } else {
+        if (!epilogue_rows<T, MODE>(ea, tacc, lane_base, (e >> 2) * half, half, nt * n_tile, blk,
+                                    [m0, M](int r) -> long { return m0 + r < M ? m0 + r : -1; }, ready)) {
+          ok = false;
+          break;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) acc = 0, acc_phase ^= 1u;
       if (MODE == 2 && p.cs_stages > 0) {
         if (lane == 0) mbar_arrive(&c_empty[cst]);
         if (++cst == p.cs_stages) cst = 0, cph ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_all();  // this warp's stores are written before the CTA leaves
   }
 
   if (!ok && p.err) atomicExch(p.err, 1);
@@ -328,7 +360,8 @@ namespace {
 constexpr size_t kSmemBudget = 227 * 1024;
 
 template <typename T, int MODE>
-cudaError_t launch(const CUtensorMap &map, const tcp::Params &p, size_t smem, cudaStream_t st) {
+cudaError_t launch(const CUtensorMap &map, const CUtensorMap &map_out, const tcp::Params &p, size_t smem,
+                   cudaStream_t st) {
   auto kern = tcp::k_tc_pw<T, MODE>;
   static unsigned long long granted = 0;
   int dev = 0;
@@ -340,7 +373,7 @@ cudaError_t launch(const CUtensorMap &map, const tcp::Params &p, size_t smem, cu
   }
   const long tiles = (long)p.m_tiles * p.n_tiles;
   const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
-  return launch_pdl(kern, dim3(grid), dim3(tcp::kThreads), smem, st, map, p);
+  return launch_pdl(kern, dim3(grid), dim3(tcp::kThreads), smem, st, map, map_out, p);
 }
 
 }  // namespace
@@ -363,6 +396,16 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // output: per-warp 32-row x 16-column boxes (rows of 64 B fp32 / 32 B bf16)
+  CUtensorMap map_out;
+  cuuint64_t odims[2] = {(cuuint64_t)op.N, (cuuint64_t)op.M};
+  cuuint64_t ostrides[1] = {(cuuint64_t)op.N * elt};
+  cuuint32_t obox[2] = {(cuuint32_t)tcx::kSliceCols, 32};
+  r = encode(&map_out, T == F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, op.dst, odims,
+             ostrides, obox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             T == F32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
 
   tcp::Params p;
   p.wimg = wimg, p.err = err, p.M = op.M;
@@ -381,7 +424,7 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.cs_ld = plan.n_tile + (plan.n_tile % 32 == 0 ? 16 : 0);
   // deepest coarse ring (2, 1 or none) that leaves at least 3 (else 2) A/B stages
   const size_t cs_stage = (size_t)tcx::kTileM * p.cs_ld * 4;
-  const size_t fixed0 = 1024 + tcx::kEpiSmem + p.bias_bytes + 8 * (3 * 8 + 8) + 16;
+  const size_t fixed0 = 1024 + tcp::kEpiPw + p.bias_bytes + 8 * (3 * 8 + 8) + 16;
   p.cs_stages = 0;
   if (op.mode == 2)
     for (int want_ab = 3; want_ab >= 2 && !p.cs_stages; want_ab--)
@@ -396,9 +439,9 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   if (stages > 6) stages = 6;
   if (stages < 2) return cudaErrorInvalidValue;
   p.stages = stages;
-  const size_t smem = stages * stage + 1024 + tcx::kEpiSmem + p.bias_bytes + p.cs_bytes + 8 * (3 * stages + 8) + 16;
-  if (T == F32) return op.mode == 0 ? launch<float, 0>(map, p, smem, st) : launch<float, 2>(map, p, smem, st);
-  return op.mode == 0 ? launch<__nv_bfloat16, 0>(map, p, smem, st) : launch<__nv_bfloat16, 2>(map, p, smem, st);
+  const size_t smem = stages * stage + 1024 + tcp::kEpiPw + p.bias_bytes + p.cs_bytes + 8 * (3 * stages + 8) + 16;
+  if (T == F32) return op.mode == 0 ? launch<float, 0>(map, map_out, p, smem, st) : launch<float, 2>(map, map_out, p, smem, st);
+  return op.mode == 0 ? launch<__nv_bfloat16, 0>(map, map_out, p, smem, st) : launch<__nv_bfloat16, 2>(map, map_out, p, smem, st);
 }
 
 }  // namespace gpu
