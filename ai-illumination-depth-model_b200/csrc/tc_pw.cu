@@ -55,40 +55,87 @@ struct Params {
 
 // Lateral: the bilinear 2x upsample (refUpsample2, reference.ts:161-193:
 // source coordinate (i + 0.5) / 2 - 0.5, both taps from the unclamped floor,
-// clamped independently) of the coarse map for tile row `r` (pixel m0 + r),
-// columns [n0, n0 + n_tile) of N, into row r of `cs`.
+// clamped independently) of the coarse map for the tile's 128 rows (pixels
+// m0 ..) and columns [n0, n0 + n_tile) of N, into `cs` (row stride cs_ld).
+// Work item = (run of 8 consecutive tile rows, 4-column group); threads take
+// items with the column group fastest, so a warp's loads of one coarse pixel
+// are contiguous. A run inside one output row starting at an even x needs
+// coarse columns x/2 - 1 .. x/2 + 4 (clamped) of two coarse rows: its 12
+// loads are issued together and each pixel combines its four taps with the
+// reference's weights and expression. Other runs (row ends, odd widths) take
+// the taps per pixel.
 template <typename T>
-__device__ __forceinline__ void coarse_row(const EpiArgs &a, long M, long m0, int r, int n0, int n_tile, float *cs,
-                                           int cs_ld) {
-  const long m = m0 + r;
-  if (m >= M) return;
+__device__ __forceinline__ void coarse_tile(const EpiArgs &a, long M, long m0, int n0, int n_tile, float *cs,
+                                            int cs_ld, int ct, int nthreads) {
   const T *coarse = reinterpret_cast<const T *>(a.coarse);
-  const uint32_t um = (uint32_t)m, uow = (uint32_t)a.OW, uoh = (uint32_t)a.OH;
-  const uint32_t t = um / uow;
-  const int x = (int)(um - t * uow);
-  const uint32_t bb = t / uoh;
-  const int y = (int)(t - bb * uoh), b = (int)bb;
-  const int CH = a.OH >> 1, CW = a.OW >> 1;
-  const float sy = (y + 0.5f) * 0.5f - 0.5f, sx = (x + 0.5f) * 0.5f - 0.5f;
-  const float fy0 = floorf(sy), fx0 = floorf(sx), fy = sy - fy0, fx = sx - fx0;
-  const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
-  const int x0 = min(max((int)fx0, 0), CW - 1), x1 = min(max((int)fx0 + 1, 0), CW - 1);
-  const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
-  const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
-  const T *p00 = coarse + (rr0 + x0) * a.N, *p01 = coarse + (rr0 + x1) * a.N;
-  const T *p10 = coarse + (rr1 + x0) * a.N, *p11 = coarse + (rr1 + x1) * a.N;
-  float *row = cs + (size_t)r * cs_ld;
   const int ncol = min(n_tile, a.N - n0);
-#pragma unroll 4
-  for (int c = 0; c < ncol; c += 4) {
-    const int n = n0 + c;
-    const float4 c00 = ld4(p00 + n), c01 = ld4(p01 + n), c10 = ld4(p10 + n), c11 = ld4(p11 + n);
-    float4 o;
-    o.x = c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
-    o.y = c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
-    o.z = c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
-    o.w = c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
-    *reinterpret_cast<float4 *>(row + c) = o;
+  const int nchunks = ncol / 4;
+  const int CH = a.OH >> 1, CW = a.OW >> 1;
+  const uint32_t uow = (uint32_t)a.OW, uoh = (uint32_t)a.OH;
+  for (int item = ct; item < 16 * nchunks; item += nthreads) {
+    const int run = item / nchunks, c4 = item - run * nchunks;
+    const int r0 = run * 8;
+    const long mA = m0 + r0;
+    if (mA >= M) continue;
+    const int n = n0 + c4 * 4;
+    const uint32_t um = (uint32_t)mA;
+    const uint32_t t = um / uow;
+    const int x = (int)(um - t * uow);
+    const uint32_t bb = t / uoh;
+    const int y = (int)(t - bb * uoh), b = (int)bb;
+    const float sy = (y + 0.5f) * 0.5f - 0.5f;
+    const float fy0 = floorf(sy), fy = sy - fy0;
+    const int y0 = min(max((int)fy0, 0), CH - 1), y1 = min(max((int)fy0 + 1, 0), CH - 1);
+    const long rr0 = ((long)b * CH + y0) * CW, rr1 = ((long)b * CH + y1) * CW;
+    if ((x & 1) == 0 && x + 7 < a.OW && mA + 7 < M) {
+      const int base = x / 2 - 1;
+      float4 t0[6], t1[6];
+#pragma unroll
+      for (int j = 0; j < 6; j++) {
+        const int cx = min(max(base + j, 0), CW - 1);
+        t0[j] = ld4(coarse + (rr0 + cx) * a.N + n);
+        t1[j] = ld4(coarse + (rr1 + cx) * a.N + n);
+      }
+#pragma unroll
+      for (int pp = 0; pp < 8; pp++) {
+        const int xp = x + pp;
+        const float sx = (xp + 0.5f) * 0.5f - 0.5f;
+        const float fx0 = floorf(sx), fx = sx - fx0;
+        // for even x the unclamped taps are base + (pp + 1) / 2 and the next
+        // one; the loaded column base + j already holds clamp(base + j)
+        const int l0 = (pp + 1) / 2;
+        const float w00 = (1 - fx) * (1 - fy), w01 = fx * (1 - fy), w10 = (1 - fx) * fy, w11 = fx * fy;
+        const float4 c00 = t0[l0], c01 = t0[l0 + 1], c10 = t1[l0], c11 = t1[l0 + 1];
+        float4 o;
+        o.x = c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
+        o.y = c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
+        o.z = c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
+        o.w = c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
+        *reinterpret_cast<float4 *>(cs + (size_t)(r0 + pp) * cs_ld + c4 * 4) = o;
+      }
+    } else {
+      for (int pp = 0; pp < 8 && mA + pp < M; pp++) {
+        const uint32_t ump = (uint32_t)(mA + pp);
+        const uint32_t tp = ump / uow;
+        const int xp = (int)(ump - tp * uow);
+        const uint32_t bp = tp / uoh;
+        const int yp = (int)(tp - bp * uoh);
+        const float syp = (yp + 0.5f) * 0.5f - 0.5f, sx = (xp + 0.5f) * 0.5f - 0.5f;
+        const float fyp0 = floorf(syp), fx0 = floorf(sx), fyp = syp - fyp0, fx = sx - fx0;
+        const int ya = min(max((int)fyp0, 0), CH - 1), yb = min(max((int)fyp0 + 1, 0), CH - 1);
+        const int xa = min(max((int)fx0, 0), CW - 1), xb = min(max((int)fx0 + 1, 0), CW - 1);
+        const long q0 = ((long)bp * CH + ya) * CW, q1 = ((long)bp * CH + yb) * CW;
+        const float w00 = (1 - fx) * (1 - fyp), w01 = fx * (1 - fyp), w10 = (1 - fx) * fyp, w11 = fx * fyp;
+        const float4 c00 = ld4(coarse + (q0 + xa) * a.N + n), c01 = ld4(coarse + (q0 + xb) * a.N + n);
+        const float4 c10 = ld4(coarse + (q1 + xa) * a.N + n), c11 = ld4(coarse + (q1 + xb) * a.N + n);
+        float4 o;
+        o.x = c00.x * w00 + c01.x * w01 + c10.x * w10 + c11.x * w11;
+        o.y = c00.y * w00 + c01.y * w01 + c10.y * w10 + c11.y * w11;
+        o.z = c00.z * w00 + c01.z * w01 + c10.z * w10 + c11.z * w11;
+        o.w = c00.w * w00 + c01.w * w01 + c10.w * w10 + c11.w * w11;
+        *reinterpret_cast<float4 *>(cs + (size_t)(r0 + pp) * cs_ld + c4 * 4) = o;
+      }
+    }
   }
 }
 
@@ -227,14 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
         if (!ok) break;
       }
       if (ring) {
-        // one tile row per thread, ahead of the epilogue
+        // (8-row run, 4-column group) items, ahead of the epilogue
         if (!__all_sync(0xffffffffu, mbar_wait(&c_empty[cst], cph ^ 1u))) {
           ok = false;
           break;
         }
         const int mt = t / p.n_tiles, nt = t % p.n_tiles;
-        coarse_row<T>(p.epi, p.M, (long)mt * kTileM, ct, nt * n_tile, n_tile, cs_smem + cst * kTileM * p.cs_ld,
-                      p.cs_ld);
+        coarse_tile<T>(p.epi, p.M, (long)mt * kTileM, nt * n_tile, n_tile, cs_smem + cst * kTileM * p.cs_ld, p.cs_ld,
+                       ct, kNumConv * 32);
         __syncwarp();
         if (lane == 0) mbar_arrive(&c_full[cst]);
         if (++cst == p.cs_stages) cst = 0, cph ^= 1u;
