@@ -130,7 +130,8 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                : "memory");
 }
 // One 128-byte slab of K for a 128 x N tile: 4 MMAs of K = 32 bytes; fp32
-// storage issues the 4 TF32 cross products of the hi/lo split (small terms first).
+// storage issues three TF32 cross products of the hi/lo split (3xTF32: the
+// lo x lo term, ~2^-22 of the product, is dropped), small terms first.
 template <bool F32>
 __device__ __forceinline__ void mma_slab(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
                                          uint32_t idesc, bool first) {
@@ -139,8 +140,7 @@ __device__ __forceinline__ void mma_slab(uint32_t d, uint32_t a_hi, uint32_t a_l
     const uint32_t ko = kk * 32;
     const uint32_t acc = (first && kk == 0) ? 0u : 1u;
     if (F32) {
-      mma_tf32(d, smem_desc(a_lo + ko), smem_desc(b_lo + ko), idesc, acc);
-      mma_tf32(d, smem_desc(a_lo + ko), smem_desc(b_hi + ko), idesc, 1u);
+      mma_tf32(d, smem_desc(a_lo + ko), smem_desc(b_hi + ko), idesc, acc);
       mma_tf32(d, smem_desc(a_hi + ko), smem_desc(b_lo + ko), idesc, 1u);
       mma_tf32(d, smem_desc(a_hi + ko), smem_desc(b_hi + ko), idesc, 1u);
     } else {
