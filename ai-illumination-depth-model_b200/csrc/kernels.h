@@ -28,6 +28,23 @@ constexpr int kBilateralArgCount = 12, kBilateralDstArg = 9;
 cudaError_t preprocess(int T, const float *frames, int layout, int n, int S, const PreprocessParams &p,
                        void *input, float *luma, float *scene, cudaStream_t st);
 
+// Preprocess fused into the stem conv (3x3, stride 2, 4 -> 16 channels, zero
+// padding): frames -> stem output dst (n, S/2, S/2, 16) and luma, plus scene
+// and the normalised input when those are non-null. Packed weights
+// [3][3][4][16], bias [16].
+struct StemParams {
+  int layout, S, OH, OW, tiles_x, tiles_y, act;
+  PreprocessParams pre;
+  const float *w, *bias;
+  void *dst;
+  float *luma, *scene;
+  void *input;
+};
+constexpr int kStemArgCount = 2, kStemFramesArg = 0;  // k_stem_fused(frames, StemParams)
+cudaError_t stem_fused(int T, const float *frames, int layout, int n, int S, const PreprocessParams &pre,
+                       const float *wpk, const float *bias, int act, void *dst, float *luma, float *scene, void *input,
+                       cudaStream_t st);
+
 // Dense conv: src (n,H,W,Cin) -> dst (n,OH,OW,Cout); packed weights [k][k][Cin][Cout].
 cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const float *wpk, const float *bias,
                  int Cout, int k, int stride, int act, void *dst, cudaStream_t st);

@@ -18,6 +18,7 @@
 
 #include <cstdint>
 
+#include "arith.cuh"
 #include "kernels.h"
 #include "pdl.cuh"
 
@@ -32,7 +33,7 @@ __device__ __forceinline__ float act_apply(int act, float v) {
   switch (act) {
     case 1: return fmaxf(v, 0.0f);
     case 2: return fminf(fmaxf(v, 0.0f), 6.0f);
-    case 3: return (v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)) / 6.0f;
+    case 3: return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f));
     default: return v;
   }
 }
@@ -46,6 +47,7 @@ struct Io<float> {
   static __device__ __forceinline__ void store4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
   static __device__ __forceinline__ float2 load2(const float *p) { return *reinterpret_cast<const float2 *>(p); }
   static __device__ __forceinline__ void store2(float *p, float2 v) { *reinterpret_cast<float2 *>(p) = v; }
+  static __device__ __forceinline__ float4 round4(float4 v) { return v; }
 };
 
 template <>
@@ -69,6 +71,12 @@ struct Io<__nv_bfloat16> {
   static __device__ __forceinline__ void store2(__nv_bfloat16 *p, float2 v) {
     *reinterpret_cast<__nv_bfloat162 *>(p) = __floats2bfloat162_rn(v.x, v.y);
   }
+  // the value a store4 + load4 round trip gives back
+  static __device__ __forceinline__ float4 round4(float4 v) {
+    const float2 a = __bfloat1622float2(__floats2bfloat162_rn(v.x, v.y));
+    const float2 b = __bfloat1622float2(__floats2bfloat162_rn(v.z, v.w));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
 };
 
 __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
@@ -78,8 +86,11 @@ __device__ __forceinline__ float4 f4fma(float4 a, float4 b, float4 c) {
   return make_float4(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y), fmaf(a.z, b.z, c.z), fmaf(a.w, b.w, c.w));
 }
 
+// The power is exp2(2.4 * log2(x)) on the hardware approximations (__powf,
+// within ~1e-6 relative here): the accuracy WGSL defines for the reference
+// shader's pow, at a small fraction of powf's instruction count.
 __device__ __forceinline__ float srgb_to_linear(float c) {
-  return c <= 0.04045f ? c / 12.92f : powf((c + 0.055f) / 1.055f, 2.4f);
+  return c <= 0.04045f ? c / 12.92f : __powf((c + 0.055f) / 1.055f, 2.4f);
 }
 
 static inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads - 1) / threads); }
@@ -105,6 +116,16 @@ bool &pdl_enabled() {
 // preprocess (src/model/kernels/io.ts:64-118 semantics, refPreprocess)
 // ---------------------------------------------------------------------------
 
+// One pixel: sRGB decode (optional), exposure, then the normalised network
+// input (r, g, b standardised; w = linear luma). r, g, bl come back as the
+// exposed linear colour (the scene colour).
+__device__ __forceinline__ float4 preprocess_px(float &r, float &g, float &bl, const PreprocessParams &p) {
+  if (p.decode_srgb) r = srgb_to_linear(r), g = srgb_to_linear(g), bl = srgb_to_linear(bl);
+  r *= p.exposure, g *= p.exposure, bl *= p.exposure;
+  const float l = 0.2126f * r + 0.7152f * g + 0.0722f * bl;
+  return make_float4((r - p.mean[0]) / p.std[0], (g - p.mean[1]) / p.std[1], (bl - p.mean[2]) / p.std[2], l);
+}
+
 // Parameter list mirrored by kPreprocessArgCount / kPreprocessFramesArg.
 template <typename T>
 __global__ void k_preprocess(const float *__restrict__ frames, int layout, long total, int S, PreprocessParams p,
@@ -124,10 +145,8 @@ __global__ void k_preprocess(const float *__restrict__ frames, int layout, long 
     float4 v = __ldg(reinterpret_cast<const float4 *>(frames) + idx);
     r = v.x, g = v.y, bl = v.z;
   }
-  if (p.decode_srgb) r = srgb_to_linear(r), g = srgb_to_linear(g), bl = srgb_to_linear(bl);
-  r *= p.exposure, g *= p.exposure, bl *= p.exposure;
-  float l = 0.2126f * r + 0.7152f * g + 0.0722f * bl;
-  float4 o = make_float4((r - p.mean[0]) / p.std[0], (g - p.mean[1]) / p.std[1], (bl - p.mean[2]) / p.std[2], l);
+  const float4 o = preprocess_px(r, g, bl, p);
+  const float l = o.w;
   Io<T>::store4(input + idx * 4, o);
   if (luma) luma[idx] = l;
   if (scene) reinterpret_cast<float4 *>(scene)[idx] = make_float4(r, g, bl, 1.0f);
@@ -308,6 +327,151 @@ cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const flo
                       stride, act, OH, OW, (float *)dst);
   return launch_pdl(k_conv<__nv_bfloat16>, grid, dim3(128), 0, st, (const __nv_bfloat16 *)src, n, H, W, Cin, wpk, bias,
                     Cout, k, stride, act, OH, OW, (__nv_bfloat16 *)dst);
+}
+
+// ---------------------------------------------------------------------------
+// preprocess fused into the stem (3x3 stride-2 conv, 4 -> 16 channels)
+// ---------------------------------------------------------------------------
+// One CTA = a 32 x 16 tile of stem outputs of one frame. Phase 1 preprocesses
+// the tile's input window (65 x 33 pixels with the one-pixel halo) into shared
+// memory, zero outside the frame (the conv's padding) and rounded to the
+// storage type as the unfused stem would read it back, and writes the luma
+// guide of the pixels the tile owns (its 64 x 32 interior; the scene colour
+// and the normalised input too when asked for). The network input itself
+// never reaches HBM. Phase 2: each thread computes 4 adjacent outputs x 16
+// channels from the window with k_conv's accumulation order (bias, then ky,
+// kx, input channel), the weights read as shared-memory broadcasts.
+constexpr int kStemTW = 32, kStemTH = 16, kStemWinW = 2 * kStemTW + 1, kStemWinH = 2 * kStemTH + 1;
+// one float4 of padding after every 8: a quarter-warp's reads (8 threads 8
+// window columns apart) then fall into distinct banks
+constexpr int kStemRow = kStemWinW + (kStemWinW + 7) / 8;
+constexpr int kStemTaps = 9 * 4 * 4;  // [ky][kx][cin][4 float4 of output channels]
+constexpr int kStemThreads = 128, kStemWin = kStemWinH * kStemWinW;
+constexpr int kStemBatch = (kStemWin + 2 * kStemThreads - 1) / (2 * kStemThreads);  // two batches
+constexpr size_t kStemSmem = (size_t)(kStemWinH * kStemRow + kStemTaps) * sizeof(float4);
+__device__ __forceinline__ int stem_col(int c) { return c + (c >> 3); }
+
+// Parameter list mirrored by kStemArgCount / kStemFramesArg.
+template <typename T>
+__global__ void __launch_bounds__(kStemThreads) k_stem_fused(const float *__restrict__ frames, const StemParams p) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float4 stem_sm[];
+  float4 *win = stem_sm, *wsm = stem_sm + kStemWinH * kStemRow;
+  const int tiles = p.tiles_x * p.tiles_y;
+  const int b = blockIdx.x / tiles, tile = blockIdx.x - b * tiles;
+  const int ty = tile / p.tiles_x, tx = tile - ty * p.tiles_x;
+  const int ox0 = tx * kStemTW, oy0 = ty * kStemTH;
+  const int ix0 = 2 * ox0 - 1, iy0 = 2 * oy0 - 1, S = p.S;
+  for (int i = threadIdx.x; i < kStemTaps; i += kStemThreads) wsm[i] = __ldg(reinterpret_cast<const float4 *>(p.w) + i);
+  const long plane = (long)S * S;
+  // the window's pixels in batches of kStemBatch per thread, all loads of a
+  // batch in flight before any is used
+  for (int i0 = 0; i0 < kStemWin; i0 += kStemBatch * kStemThreads) {
+    float r[kStemBatch], g[kStemBatch], bl[kStemBatch];
+#pragma unroll
+    for (int u = 0; u < kStemBatch; u++) {
+      const int i = i0 + u * kStemThreads + (int)threadIdx.x;
+      const int ry = i / kStemWinW, rx = i - ry * kStemWinW;
+      const int iy = iy0 + ry, ix = ix0 + rx;
+      r[u] = g[u] = bl[u] = 0.0f;
+      if (i < kStemWin && iy >= 0 && iy < S && ix >= 0 && ix < S) {
+        const long pix = (long)iy * S + ix;
+        if (p.layout == 0) {
+          const float *f = frames + b * 3 * plane + pix;
+          r[u] = __ldg(f), g[u] = __ldg(f + plane), bl[u] = __ldg(f + 2 * plane);
+        } else {
+          const float4 c = __ldg(reinterpret_cast<const float4 *>(frames) + b * plane + pix);
+          r[u] = c.x, g[u] = c.y, bl[u] = c.z;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kStemBatch; u++) {
+      const int i = i0 + u * kStemThreads + (int)threadIdx.x;
+      if (i >= kStemWin) break;
+      const int ry = i / kStemWinW, rx = i - ry * kStemWinW;
+      const int iy = iy0 + ry, ix = ix0 + rx;
+      float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (iy >= 0 && iy < S && ix >= 0 && ix < S) {
+        const long idx = b * plane + (long)iy * S + ix;
+        const float4 o = preprocess_px(r[u], g[u], bl[u], p.pre);
+        v = Io<T>::round4(o);
+        if (ry >= 1 && rx >= 1 && ry <= 2 * kStemTH && rx <= 2 * kStemTW) {
+          p.luma[idx] = o.w;
+          if (p.scene) reinterpret_cast<float4 *>(p.scene)[idx] = make_float4(r[u], g[u], bl[u], 1.0f);
+          if (p.input) Io<T>::store4(static_cast<T *>(p.input) + idx * 4, o);
+        }
+      }
+      win[ry * kStemRow + stem_col(rx)] = v;
+    }
+  }
+  __syncthreads();
+
+  const int ly = threadIdx.x >> 3, xg = threadIdx.x & 7;
+  const int oy = oy0 + ly, ox = ox0 + xg * 4;
+  if (oy >= p.OH || ox >= p.OW) return;
+  float4 acc[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float4 bj = __ldg(reinterpret_cast<const float4 *>(p.bias) + j);
+#pragma unroll
+    for (int q = 0; q < 4; q++) acc[q][j] = bj;
+  }
+#pragma unroll 1
+  for (int ky = 0; ky < 3; ky++) {
+    const float4 *row = win + (2 * ly + ky) * kStemRow;
+    float xs[9][4];
+#pragma unroll
+    for (int c = 0; c < 9; c++) {
+      const float4 x = row[stem_col(8 * xg + c)];
+      xs[c][0] = x.x, xs[c][1] = x.y, xs[c][2] = x.z, xs[c][3] = x.w;
+    }
+#pragma unroll
+    for (int kx = 0; kx < 3; kx++) {
+#pragma unroll
+      for (int ci = 0; ci < 4; ci++) {
+        const float4 *wr = wsm + ((ky * 3 + kx) * 4 + ci) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float4 wv = wr[j];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float x = xs[2 * q + kx][ci];
+            acc[q][j] = f4fma(make_float4(x, x, x, x), wv, acc[q][j]);
+          }
+        }
+      }
+    }
+  }
+  T *o = static_cast<T *>(p.dst) + (((long)b * p.OH + oy) * p.OW + ox) * 16;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    if (ox + q >= p.OW) break;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float4 v = acc[q][j];
+      Io<T>::store4(o + q * 16 + j * 4, make_float4(act_apply(p.act, v.x), act_apply(p.act, v.y),
+                                                    act_apply(p.act, v.z), act_apply(p.act, v.w)));
+    }
+  }
+}
+
+cudaError_t stem_fused(int T, const float *frames, int layout, int n, int S, const PreprocessParams &pre,
+                       const float *wpk, const float *bias, int act, void *dst, float *luma, float *scene, void *input,
+                       cudaStream_t st) {
+  const long total = (long)n * S * S;
+  if (total > kMaxIndex || !luma) return cudaErrorInvalidValue;
+  if (total == 0) return cudaSuccess;
+  StemParams p;
+  p.layout = layout, p.S = S;
+  p.OH = (S - 1) / 2 + 1, p.OW = p.OH;
+  p.tiles_x = (p.OW + kStemTW - 1) / kStemTW, p.tiles_y = (p.OH + kStemTH - 1) / kStemTH;
+  p.act = act, p.pre = pre, p.w = wpk, p.bias = bias, p.dst = dst, p.luma = luma, p.scene = scene, p.input = input;
+  const long blocks = (long)n * p.tiles_x * p.tiles_y;
+  if (blocks > kMaxIndex) return cudaErrorInvalidValue;
+  if (T == F32) return launch_pdl(k_stem_fused<float>, dim3((unsigned)blocks), dim3(kStemThreads), kStemSmem, st, frames, p);
+  return launch_pdl(k_stem_fused<__nv_bfloat16>, dim3((unsigned)blocks), dim3(kStemThreads), kStemSmem, st, frames, p);
 }
 
 // ---------------------------------------------------------------------------
@@ -599,11 +763,24 @@ __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh
                             float *__restrict__ out_tex) {
   pdl_wait();
   pdl_trigger();
+  // Spatial weights of quads whose 3x3 low-res taps are all inside the map:
+  // for sub-pixel (sx, sy) and tap (dx, dy) the offset is (dx - sx/2 + 1/4,
+  // dy - sy/2 + 1/4) wherever the quad is, computed exactly in binary32, so
+  // the table holds the very values the per-tap expression gives.
+  __shared__ float sp_tab[36];
+  if (threadIdx.x < 36) {
+    const int sub = threadIdx.x / 9, k = threadIdx.x - sub * 9;
+    const float dxs = (float)(k % 3 - 1) - ((float)(sub & 1) * 0.5f - 0.25f);
+    const float dys = (float)(k / 3 - 1) - ((float)(sub >> 1) * 0.5f - 0.25f);
+    sp_tab[threadIdx.x] = expf(-(dxs * dxs + dys * dys) * 0.5f);
+  }
+  __syncthreads();
   const int S = lh * 2, SW = lw * 2;
   const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= (long)n * lh * lw) return;
   int qi, qj, b;
   unflatten3(q, lw, lh, qi, qj, b);
+  const bool interior = qi >= 1 && qj >= 1 && qi + 1 < lw && qj + 1 < lh;
   auto luma_at = [&](int gx, int gy) -> float {
     const long g = ((long)b * S + gy) * SW + gx;
     if (luma) return __ldg(luma + g);
@@ -629,11 +806,21 @@ __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh
     const int x = 2 * qi + (sub & 1), y = 2 * qj + (sub >> 1);
     const float here = luma_at(x, y);
     const float cx = (x + 0.5f) * 0.5f - 0.5f, cy = (y + 0.5f) * 0.5f - 0.5f;
+    float spatial_k[9];
+    if (interior) {
+#pragma unroll
+      for (int k = 0; k < 9; k++) spatial_k[k] = sp_tab[sub * 9 + k];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 9; k++) {
+        const float dxs = tqx[k] - cx, dys = tqy[k] - cy;
+        spatial_k[k] = expf(-(dxs * dxs + dys * dys) * 0.5f);
+      }
+    }
     float weighted = 0.0f, total_w = 0.0f;
 #pragma unroll
     for (int k = 0; k < 9; k++) {
-      const float dxs = tqx[k] - cx, dys = tqy[k] - cy;
-      const float spatial = expf(-(dxs * dxs + dys * dys) * 0.5f);
+      const float spatial = spatial_k[k];
       const float dl = (here - there[k]) * inv;
       const float wgt = spatial * expf(-dl * dl * 0.5f);
       weighted = fmaf(disp[k], wgt, weighted);

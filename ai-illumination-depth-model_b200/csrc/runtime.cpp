@@ -92,6 +92,7 @@ struct GraphKey {
 // Graph nodes whose pointer arguments depend on the caller's buffers.
 struct CaptureNodes {
   cudaGraphNode_t pre = nullptr, bil = nullptr, low = nullptr;
+  int pre_nargs = 0, pre_frames_arg = 0;  // argument list of the node that reads the frames
 };
 
 struct GraphEntry {
@@ -141,6 +142,8 @@ struct illumina_model {
   int *d_err = nullptr;              // set by a kernel that gave up a bounded wait
   float *d_splitk = nullptr;         // split-K partial tiles of the tensor dw->pw kernel
   int *d_splitk_cnt = nullptr;       // its per-item arrival counters (zero between launches)
+  int stem_fused_op = -1;            // conv op folded into the preprocess launch, or -1
+  bool stem_writes_input = true;     // the folded launch still writes the network input
 
   void *tensor(const std::string &name) {
     auto it = plan.assignment.find(name);
@@ -204,6 +207,43 @@ gpu::PreprocessParams preprocess_params(const illumina_model &m) {
   return p;
 }
 
+// runner.ts:466-476: a tensor is stolen (not readable after the forward) when
+// a later op writes the buffer it was assigned.
+bool tensor_live_at_end(const illumina_model &m, const std::string &name) {
+  auto as = m.plan.assignment.find(name);
+  if (as == m.plan.assignment.end()) return false;
+  int produced = -1;
+  for (size_t i = 0; i < m.arch.ops.size(); i++)
+    if (m.arch.ops[i].out == name) {
+      produced = (int)i;
+      break;
+    }
+  for (size_t i = 0; i < m.arch.ops.size(); i++) {
+    if ((int)i <= produced) continue;
+    auto o = m.plan.assignment.find(m.arch.ops[i].out);
+    if (o != m.plan.assignment.end() && o->second == as->second) return false;
+  }
+  return true;
+}
+
+// Folds the stem into the preprocess launch when the preprocess output's only
+// reader is the op right after it, a 3x3 stride-2 conv from 4 to 16 channels.
+// The input tensor is then written only when it is readable after the forward
+// (kept intermediates, or a buffer no later op reuses).
+void plan_stem_fusion(illumina_model &m) {
+  m.stem_fused_op = -1;
+  const auto &ops = m.arch.ops;
+  if (ops.size() < 2 || ops[0].kind != OpKind::Preprocess) return;
+  const Op &c = ops[1];
+  if (c.kind != OpKind::Conv || c.in != ops[0].out || c.k != 3 || c.stride != 2) return;
+  if (m.arch.shape(c.in).c != 4 || m.arch.shape(c.out).c != 16) return;
+  for (size_t i = 2; i < ops.size(); i++)
+    for (const auto &t : op_inputs(ops[i]))
+      if (t == ops[0].out) return;
+  m.stem_fused_op = 1;
+  m.stem_writes_input = m.opts.keep_intermediates != 0 || tensor_live_at_end(m, ops[0].out);
+}
+
 // Enqueues the whole op list on m.stream. mode 0: independent frames -> disp;
 // mode 1: streaming frame with history (n == 1).
 // The node most recently added to the graph being captured on `st`.
@@ -234,13 +274,30 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
   for (size_t i = 0; i < a.ops.size(); i++) {
     const Op &op = a.ops[i];
     if (marks) cuda_check(cudaEventRecord((*marks)[i], st), "profile event");
+    if ((int)i == m.stem_fused_op) continue;  // ran inside the preprocess launch
     const OpWeights &w = m.opw[i];
     switch (op.kind) {
       case OpKind::Preprocess:
-        cuda_check(gpu::preprocess(m.T, frames, layout, n, S, preprocess_params(m), m.tensor(op.out), m.d_luma,
-                                   m.d_scene, st),
-                   "preprocess");
-        if (nodes) nodes->pre = last_captured_node(st);
+        if (m.stem_fused_op >= 0) {
+          // preprocess + stem in one kernel; the network input is written only
+          // when it stays readable after the forward
+          const Op &stem = a.ops[m.stem_fused_op];
+          const OpWeights &sw = m.opw[m.stem_fused_op];
+          cuda_check(gpu::stem_fused(m.T, frames, layout, n, S, preprocess_params(m), sw.w, sw.b, stem.act,
+                                     m.tensor(stem.out), m.d_luma, m.d_scene,
+                                     m.stem_writes_input ? m.tensor(op.out) : nullptr, st),
+                     "preprocess+stem");
+          if (nodes)
+            nodes->pre = last_captured_node(st), nodes->pre_nargs = gpu::kStemArgCount,
+            nodes->pre_frames_arg = gpu::kStemFramesArg;
+        } else {
+          cuda_check(gpu::preprocess(m.T, frames, layout, n, S, preprocess_params(m), m.tensor(op.out), m.d_luma,
+                                     m.d_scene, st),
+                     "preprocess");
+          if (nodes)
+            nodes->pre = last_captured_node(st), nodes->pre_nargs = gpu::kPreprocessArgCount,
+            nodes->pre_frames_arg = gpu::kPreprocessFramesArg;
+        }
         launches++;
         break;
       case OpKind::Conv: {
@@ -338,7 +395,7 @@ GraphEntry &graph_for(illumina_model &m, const GraphKey &key, const float *frame
   for (auto &g : m.graphs) {
     if (!(g.key == key)) continue;
     if (g.frames != frames) {
-      patch_kernel_arg(g, g.nodes.pre, gpu::kPreprocessArgCount, gpu::kPreprocessFramesArg, frames);
+      patch_kernel_arg(g, g.nodes.pre, g.nodes.pre_nargs, g.nodes.pre_frames_arg, frames);
       g.frames = frames;
     }
     if (g.disp != disp) {
@@ -473,6 +530,7 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
   std::vector<std::string> exclude = {"depth"};
   m.plan = plan_arena(m.arch, exclude, o.keep_intermediates != 0);
   validate_arena(m.arch, m.plan, exclude);
+  plan_stem_fusion(m);
 
   // --- device ---
   int ndev = 0;
@@ -840,20 +898,7 @@ illumina_status illumina_model_debug_tensor(illumina_model *m, const char *name,
   if (h) *h = s.h;
   if (w) *w = s.w;
   if (c) *c = s.c;
-  // runner.ts:466-476: stolen if any later op writes the same buffer.
-  int produced = -1;
-  for (size_t i = 0; i < m->arch.ops.size(); i++)
-    if (m->arch.ops[i].out == n) {
-      produced = (int)i;
-      break;
-    }
-  bool stolen = false;
-  for (size_t i = 0; i < m->arch.ops.size(); i++) {
-    if ((int)i <= produced) continue;
-    auto o = m->plan.assignment.find(m->arch.ops[i].out);
-    if (o != m->plan.assignment.end() && o->second == as->second) stolen = true;
-  }
-  if (live_at_end) *live_at_end = stolen ? 0 : 1;
+  if (live_at_end) *live_at_end = tensor_live_at_end(*m, n) ? 1 : 0;
   if (!out) return ILLUMINA_OK;
   cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
   long count = s.elems();

@@ -9,6 +9,8 @@
 
 #include <cstdint>
 
+#include "arith.cuh"
+
 namespace illumina {
 namespace gpu {
 namespace tcx {
@@ -170,18 +172,6 @@ __device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
   hi = tf32_round(x);
   lo = tf32_round(x - __uint_as_float(hi));
 }
-// a / 6 rounded to nearest binary32 without the branches of the IEEE divide
-// sequence (which serialise the many independent divisions of an epilogue
-// block or a depthwise run). The product a * RN64(1/6) in binary64 is within
-// 2^-53 relative of the exact quotient, and the quotient can never lie that
-// close to a binary32 rounding midpoint: a / 6 is either exactly
-// representable or has the periodic binary expansion of a third, whose digits
-// beyond any binary32 precision (normal or subnormal) are 0101... or 1010...,
-// at least 1/6 ulp away from the midpoint pattern 1000.... So rounding the
-// binary64 product to binary32 gives RN(a / 6). (A binary32 FMA-corrected
-// quotient with a guard for tiny inputs measured slower.) illumina_selftest
-// checks it bit for bit against a / 6.0f over every non-NaN binary32 input.
-__device__ __forceinline__ float div6(float a) { return __double2float_rn((double)a * (1.0 / 6.0)); }
 __device__ __forceinline__ float hardswish(float v) { return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)); }
 __device__ __forceinline__ float act_apply(int act, float v) {
   switch (act) {

@@ -98,7 +98,9 @@ def test_network64_aliased_arena_live_at_end(torch, net64):
     _, live_in = m.debugTensor("input")
     assert not live_in  # the arena recycles `input` right after the stem (network.test.ts:81-84)
     s = m.stats
-    assert s.dispatches == 40 and s.launches == 40 and s.deviceError == 0
+    # 40 ops (the reference's dispatch count); the stem runs inside the
+    # preprocess launch, so 39 kernel launches
+    assert s.dispatches == 40 and s.launches == 39 and s.deviceError == 0
     assert abs(s.arenaBytes - 19.03e6 / 49) < 1e5 or s.arenaBytes < s.naiveArenaBytes
     m.destroy()
 
