@@ -167,10 +167,14 @@ __device__ __forceinline__ uint32_t tf32_rna(float x) {
 // the dropped part is at least one half ulp. illumina_selftest compares it
 // with cvt.rna.tf32.f32 over every non-NaN binary32 input.
 __device__ __forceinline__ uint32_t tf32_round(float x) { return (__float_as_uint(x) + 0x1000u) & 0xffffe000u; }
-// x = hi + lo with hi, lo exact TF32 values, both rounded to nearest.
+// x = hi + lo exactly: hi = x rounded to the nearest TF32 value, lo the
+// binary32 remainder (at most 13 significant bits). The kind::tf32 MMA reads
+// lo at TF32 precision (its low 13 bits dropped), so the operand it sees is
+// within 2^-21 |x| of x (2^-22 if lo were rounded too, at two more
+// instructions per element).
 __device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
   hi = tf32_round(x);
-  lo = tf32_round(x - __uint_as_float(hi));
+  lo = __float_as_uint(x - __uint_as_float(hi));
 }
 __device__ __forceinline__ float hardswish(float v) { return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)); }
 __device__ __forceinline__ float act_apply(int act, float v) {

@@ -11,7 +11,7 @@
 // Roles inside one CTA (480 threads, one CTA per SM, items strided by grid):
 //   warp 0        halo producer: per (item, slab) one 4-D TMA load of the
 //                 input halo ((th-1)*S+KS rows x (tw-1)*S+KS columns x one
-//                 slab, SWIZZLE_128B; coordinates outside the frame read as
+//                 slab, unswizzled; coordinates outside the frame read as
 //                 zero, which is the depthwise zero padding) plus a bulk copy
 //                 of the slab's depthwise taps and bias into the `H` ring.
 //   warp 14       weight producer: bulk copies of the pre-swizzled pointwise
@@ -245,7 +245,7 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = encode(&map, T == F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
                       const_cast<void *>(op.src), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   // output: 16-column slices of a th x tw patch, rows of 64 B (fp32) or 32 B

@@ -11,7 +11,7 @@
 // Roles inside one CTA (480 threads, one CTA per SM, items strided by grid):
 //   warp 0        halo producer: per (item, slab) one 4-D TMA load of the
 //                 input halo ((th-1)*S+KS rows x (tw-1)*S+KS columns x one
-//                 slab, SWIZZLE_128B; coordinates outside the frame read as
+//                 slab, unswizzled; coordinates outside the frame read as
 //                 zero, which is the depthwise zero padding) plus a bulk copy
 //                 of the slab's depthwise taps and bias into the `H` ring.
 //   warp 14       weight producer: bulk copies of the pre-swizzled pointwise
@@ -106,13 +106,16 @@ __device__ __forceinline__ Item decode(const Params &p, int u) {
   return it;
 }
 
-// Four channels (group `cg`) of halo pixel R: the TMA wrote 128-byte rows with
-// the 16-byte chunk c of row R at chunk position c ^ (R & 7).
+// Four channels (group `cg`) of halo pixel R: the TMA wrote one unswizzled
+// 128-byte row per pixel. The eight (fp32) or sixteen (bf16) threads that
+// read one pixel's row cover it once, so a warp's read takes the minimum
+// number of shared-memory wavefronts, and every tap's address is the
+// thread's base plus a constant.
 __device__ __forceinline__ float4 halo_ld(const float *, const uint8_t *halo, int R, int cg) {
-  return *reinterpret_cast<const float4 *>(halo + R * 128 + ((cg ^ (R & 7)) << 4));
+  return *reinterpret_cast<const float4 *>(halo + R * 128 + (cg << 4));
 }
 __device__ __forceinline__ float4 halo_ld(const __nv_bfloat16 *, const uint8_t *halo, int R, int cg) {
-  const uint2 v = *reinterpret_cast<const uint2 *>(halo + R * 128 + (((cg >> 1) ^ (R & 7)) << 4) + ((cg & 1) << 3));
+  const uint2 v = *reinterpret_cast<const uint2 *>(halo + R * 128 + (cg << 3));
   const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v.x));
   const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v.y));
   return make_float4(a.x, a.y, b.x, b.y);
