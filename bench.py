@@ -188,13 +188,14 @@ def op_algorithmic(arch, cost, elt=4):
             b = (SIZE * SIZE * 3 + e(op.out)) * 4
         elif op.kind == "bilateralUp":
             low = t[op.inp]
-            b = (low.h * low.w + SIZE * SIZE * 3 + SIZE * SIZE) * 4
+            b = (low.h * low.w + SIZE * SIZE + SIZE * SIZE) * 4  # low-res map, luma guide, output
         elif op.kind == "head":
             b = (e(op.inp) + t[op.out].h * t[op.out].w) * elt
         elif op.kind == "lateral":
             b = (e(op.coarse) + e(op.skip) + e(op.out)) * elt
         else:
-            ins = [op.inp] + ([op.residual] if op.residual else [])
+            # a residual that is the op's own input (d0.refine) is read once
+            ins = [op.inp] + ([op.residual] if op.residual and op.residual != op.inp else [])
             b = (sum(e(n) for n in ins) + e(op.out)) * elt
         out[op.name] = (b, 2 * c.macs)
     return out
