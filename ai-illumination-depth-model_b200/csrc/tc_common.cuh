@@ -18,6 +18,10 @@ namespace tcx {
 constexpr int kTileM = 128;
 constexpr uint32_t kAImage = kTileM * 128;  // one 128-row x 128-byte operand image
 constexpr long long kWaitCycles = 1ll << 31;
+// A waiting thread stays suspended in try_wait until the phase completes or
+// this many nanoseconds pass, instead of re-polling at the hardware's default
+// interval (polling warps take issue slots from the working ones).
+constexpr uint32_t kSuspendNs = 20000;
 constexpr int kEpiWarps = 8;                // 2 per TMEM lane quarter (column halves)
 constexpr int kEpiCols = 16;                // accumulator columns per transpose block
 constexpr int kEpiStride = 20;              // floats per row of a block (16 + 4 pad: conflict-free)
@@ -32,9 +36,9 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
