@@ -88,9 +88,11 @@ __device__ __forceinline__ float4 f4fma(float4 a, float4 b, float4 c) {
 
 // The power is exp2(2.4 * log2(x)) on the hardware approximations (__powf,
 // within ~1e-6 relative here): the accuracy WGSL defines for the reference
-// shader's pow, at a small fraction of powf's instruction count.
+// shader's pow, at a small fraction of powf's instruction count. The
+// divisions by constants are products with the rounded reciprocals (within
+// 1.5 ulp of the quotient; WGSL gives its division 2.5 ulp).
 __device__ __forceinline__ float srgb_to_linear(float c) {
-  return c <= 0.04045f ? c / 12.92f : __powf((c + 0.055f) / 1.055f, 2.4f);
+  return c <= 0.04045f ? c * (1.0f / 12.92f) : __powf((c + 0.055f) * (1.0f / 1.055f), 2.4f);
 }
 
 static inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads - 1) / threads); }
@@ -117,13 +119,15 @@ bool &pdl_enabled() {
 // ---------------------------------------------------------------------------
 
 // One pixel: sRGB decode (optional), exposure, then the normalised network
-// input (r, g, b standardised; w = linear luma). r, g, bl come back as the
+// input (r, g, b standardised with the rounded reciprocal of std; w = linear
+// luma). r, g, bl come back as the
 // exposed linear colour (the scene colour).
 __device__ __forceinline__ float4 preprocess_px(float &r, float &g, float &bl, const PreprocessParams &p) {
   if (p.decode_srgb) r = srgb_to_linear(r), g = srgb_to_linear(g), bl = srgb_to_linear(bl);
   r *= p.exposure, g *= p.exposure, bl *= p.exposure;
   const float l = 0.2126f * r + 0.7152f * g + 0.0722f * bl;
-  return make_float4((r - p.mean[0]) / p.std[0], (g - p.mean[1]) / p.std[1], (bl - p.mean[2]) / p.std[2], l);
+  return make_float4((r - p.mean[0]) * p.inv_std[0], (g - p.mean[1]) * p.inv_std[1], (bl - p.mean[2]) * p.inv_std[2],
+                     l);
 }
 
 // Parameter list mirrored by kPreprocessArgCount / kPreprocessFramesArg.
