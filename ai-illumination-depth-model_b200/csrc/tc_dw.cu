@@ -276,6 +276,10 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.ws = op.ws, p.cnt = op.ws_cnt;
   p.tw = tl.tw, p.th = tl.th, p.iw = tl.iw, p.mid_act = op.mid_act;
   p.sh = tl.sh, p.sg = tl.sg, p.b_res = tl.b_res, p.ng = tl.ng;
+  // a second epilogue team (one per TMEM accumulator, so two items'
+  // epilogues run at once) when its buffers fit beside the planned rings
+  p.teams = tl.ksplit == 1 && tl.smem + tcd::kEpiBytes <= kSmemBudget ? 2 : 1;
+  const size_t smem = tl.smem + (p.teams - 1) * tcd::kEpiBytes;
   p.halo_bytes = (uint32_t)(tl.iw * tl.ih * 128);
   p.dw_bytes = (uint32_t)((op.ks * op.ks + 1) * slab_c * 4);
   p.h_stage = (uint32_t)align_to(p.halo_bytes + p.dw_bytes, 1024);
@@ -287,10 +291,10 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.bias_bytes = (uint32_t)align_to((size_t)op.N * 4, 16);
   const bool split = tl.ksplit > 1;
   if (T == F32)
-    return split ? tcd::launch_all<float, true>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st)
-                 : tcd::launch_all<float, false>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st);
-  return split ? tcd::launch_all<__nv_bfloat16, true>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st)
-               : tcd::launch_all<__nv_bfloat16, false>(op.ks, op.stride, tl.P, map, map_out, p, tl.smem, st);
+    return split ? tcd::launch_all<float, true>(op.ks, op.stride, tl.P, map, map_out, p, smem, st)
+                 : tcd::launch_all<float, false>(op.ks, op.stride, tl.P, map, map_out, p, smem, st);
+  return split ? tcd::launch_all<__nv_bfloat16, true>(op.ks, op.stride, tl.P, map, map_out, p, smem, st)
+               : tcd::launch_all<__nv_bfloat16, false>(op.ks, op.stride, tl.P, map, map_out, p, smem, st);
 }
 
 }  // namespace gpu

@@ -57,12 +57,28 @@ namespace tcd {
 
 using namespace tcx;
 
-constexpr int kMmaWarp = 1, kXfWarp0 = 2, kGroupWarps = 4, kMaxGroups = 2, kEpiWarp0 = 10, kEpiW = 4,
-              kBWarp = 14;
-constexpr int kThreads = 32 * (kBWarp + 1);
-// one pair of TMA-store slice buffers, or the transposed-store blocks of wide tiles
+// Warpgroups: 0 = producers and MMA (warps 0-3), 1-2 = depthwise groups,
+// 3-4 = epilogue teams (one per TMEM accumulator). Registers are moved from
+// the producer and epilogue warpgroups to the depthwise ones with setmaxnreg:
+// 4 x 32 x 32 + 8 x 32 x 136 + 8 x 32 x 88 = 61440 = 640 threads x 96.
+constexpr int kMmaWarp = 1, kBWarp = 2, kXfWarp0 = 4, kGroupWarps = 4, kMaxGroups = 2, kEpiWarp0 = 12, kEpiW = 4,
+              kEpiTeams = 2;
+constexpr int kThreads = 32 * (kEpiWarp0 + kEpiTeams * kEpiW);
+constexpr int kLaunchRegs = 96, kProducerRegs = 32, kXfRegs = 136, kEpiRegs = 88;
+static_assert(128 * kProducerRegs + 256 * kXfRegs + 256 * kEpiRegs <= kThreads * kLaunchRegs, "register split");
+// per epilogue team: one pair of TMA-store slice buffers, or the
+// transposed-store blocks of wide tiles
 constexpr uint32_t kEpiBytes = 2 * kSliceBytes > kEpiW * 32 * kEpiStride * 4 ? 2 * kSliceBytes
                                                                              : kEpiW * 32 * kEpiStride * 4;
+
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 struct Params {
   const uint8_t *wimg;   // pointwise images [n tile][slab], b_bytes each
@@ -74,6 +90,7 @@ struct Params {
   int tiles_x, tiles_y, n_tiles, slabs, items, ksplit, spk, total;  // total = items * ksplit units
   int tw, th, iw, mid_act;
   int sh, sg, b_res, ng;
+  int teams;  // epilogue teams: 2 = one per accumulator, 1 = team 0 takes every item
   uint32_t halo_bytes, dw_bytes, h_stage, g_stage, b_bytes, acc_stride, tmem_cols, bias_bytes;
 };
 
@@ -210,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
   uint8_t *bres = gbase + p.sg * p.g_stage;
   const uint32_t res_bytes = p.b_res ? (uint32_t)(p.n_tiles * p.slabs) * p.b_bytes : 0u;
   float *epi_smem = reinterpret_cast<float *>(bres + res_bytes);
-  float *bias_smem = epi_smem + kEpiBytes / 4;
+  float *bias_smem = epi_smem + p.teams * kEpiBytes / 4;
   uint64_t *h_full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(bias_smem) + p.bias_bytes);
   uint64_t *h_empty = h_full + p.sh;
   uint64_t *g_full = h_empty + p.sh;
@@ -252,102 +269,106 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
-  if (warp == 0) {
-    // ------------------------------------------------------- halo producer
-    if (lane == 0) {
-      pdl_wait();  // the input is the previous kernel's output
-      int hs = 0;
-      uint32_t hph = 0;
-      long issued = 0;
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
-        const Item it = decode<SPLIT>(p, t);
-        for (int s = it.s0; s < it.s1; s++) {
-          if (!mbar_wait(&h_empty[hs], hph ^ 1u)) {
-            ok = false;
-            break;
-          }
-          uint8_t *hst = hbase + (size_t)hs * p.h_stage;
-          mbar_expect_tx(&h_full[hs], p.halo_bytes + p.dw_bytes);
-          tma_load_4d(smem_u32(hst), &tmap, s * kSlabC, it.x0 * S - kPad, it.y0 * S - kPad, it.b, &h_full[hs]);
-          bulk_load(smem_u32(hst + p.halo_bytes), p.dwblk + (size_t)s * p.dw_bytes, p.dw_bytes, &h_full[hs]);
-          issued++;
-          if (++hs == p.sh) hs = 0, hph ^= 1u;
-        }
-      }
-      // every copy issued above lands before the CTA may leave
-      for (long i = issued > p.sh ? issued - p.sh : 0; i < issued; i++)
-        ok = mbar_wait(&h_full[i % p.sh], (uint32_t)((i / p.sh) & 1)) && ok;
-    }
-  } else if (warp == kBWarp) {
-    // ------------------------------------------------------- weight producer
-    if (lane == 0) {
-      if (p.b_res) {
-        mbar_expect_tx(b_full, res_bytes);
-        for (int i = 0; i < p.n_tiles * p.slabs; i++)
-          bulk_load(smem_u32(bres + (size_t)i * p.b_bytes), p.wimg + (size_t)i * p.b_bytes, p.b_bytes, b_full);
-        ok = mbar_wait(b_full, 0);
-      } else {
-        int gs = 0;
-        uint32_t gph = 0;
+  if (warp < kXfWarp0) {
+    reg_dealloc<kProducerRegs>();
+    if (warp == 0) {
+      // ------------------------------------------------------- halo producer
+      if (lane == 0) {
+        pdl_wait();  // the input is the previous kernel's output
+        int hs = 0;
+        uint32_t hph = 0;
         long issued = 0;
         for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
           const Item it = decode<SPLIT>(p, t);
-          const int nt = it.nt;
           for (int s = it.s0; s < it.s1; s++) {
-            if (!mbar_wait(&g_empty[gs], gph ^ 1u)) {
+            if (!mbar_wait(&h_empty[hs], hph ^ 1u)) {
               ok = false;
               break;
             }
-            mbar_expect_tx(&g_full[gs], p.b_bytes);
-            bulk_load(smem_u32(gbase + (size_t)gs * p.g_stage + kTerms * kAImage),
-                      p.wimg + ((size_t)nt * p.slabs + s) * p.b_bytes, p.b_bytes, &g_full[gs]);
+            uint8_t *hst = hbase + (size_t)hs * p.h_stage;
+            mbar_expect_tx(&h_full[hs], p.halo_bytes + p.dw_bytes);
+            tma_load_4d(smem_u32(hst), &tmap, s * kSlabC, it.x0 * S - kPad, it.y0 * S - kPad, it.b, &h_full[hs]);
+            bulk_load(smem_u32(hst + p.halo_bytes), p.dwblk + (size_t)s * p.dw_bytes, p.dw_bytes, &h_full[hs]);
             issued++;
-            if (++gs == p.sg) gs = 0, gph ^= 1u;
+            if (++hs == p.sh) hs = 0, hph ^= 1u;
           }
         }
-        for (long i = issued > p.sg ? issued - p.sg : 0; i < issued; i++)
-          ok = mbar_wait(&g_full[i % p.sg], (uint32_t)((i / p.sg) & 1)) && ok;
+        // every copy issued above lands before the CTA may leave
+        for (long i = issued > p.sh ? issued - p.sh : 0; i < issued; i++)
+          ok = mbar_wait(&h_full[i % p.sh], (uint32_t)((i / p.sh) & 1)) && ok;
       }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      if (p.b_res && !mbar_wait(b_full, 0)) ok = false;
-      int gs = 0, acc = 0;
-      uint32_t gph = 0, acc_phase = 0;
-      const uint32_t idesc = instr_desc(kF32 ? 2u : 1u, (uint32_t)n_tile);
-      const uint32_t b_img = (uint32_t)n_tile * 128u;
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
-        const Item it = decode<SPLIT>(p, t);
-        const int nt = it.nt;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u)) {
-          ok = false;
-          break;
+    } else if (warp == kBWarp) {
+      // ------------------------------------------------------- weight producer
+      if (lane == 0) {
+        if (p.b_res) {
+          mbar_expect_tx(b_full, res_bytes);
+          for (int i = 0; i < p.n_tiles * p.slabs; i++)
+            bulk_load(smem_u32(bres + (size_t)i * p.b_bytes), p.wimg + (size_t)i * p.b_bytes, p.b_bytes, b_full);
+          ok = mbar_wait(b_full, 0);
+        } else {
+          int gs = 0;
+          uint32_t gph = 0;
+          long issued = 0;
+          for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
+            const Item it = decode<SPLIT>(p, t);
+            const int nt = it.nt;
+            for (int s = it.s0; s < it.s1; s++) {
+              if (!mbar_wait(&g_empty[gs], gph ^ 1u)) {
+                ok = false;
+                break;
+              }
+              mbar_expect_tx(&g_full[gs], p.b_bytes);
+              bulk_load(smem_u32(gbase + (size_t)gs * p.g_stage + kTerms * kAImage),
+                        p.wimg + ((size_t)nt * p.slabs + s) * p.b_bytes, p.b_bytes, &g_full[gs]);
+              issued++;
+              if (++gs == p.sg) gs = 0, gph ^= 1u;
+            }
+          }
+          for (long i = issued > p.sg ? issued - p.sg : 0; i < issued; i++)
+            ok = mbar_wait(&g_full[i % p.sg], (uint32_t)((i / p.sg) & 1)) && ok;
         }
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)acc * p.acc_stride;
-        for (int s = it.s0; s < it.s1; s++) {
-          if (!mbar_wait(&a_ready[gs], gph) || (!p.b_res && !mbar_wait(&g_full[gs], gph))) {
+      }
+    } else if (warp == kMmaWarp) {
+      // ------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        if (p.b_res && !mbar_wait(b_full, 0)) ok = false;
+        int gs = 0, acc = 0;
+        uint32_t gph = 0, acc_phase = 0;
+        const uint32_t idesc = instr_desc(kF32 ? 2u : 1u, (uint32_t)n_tile);
+        const uint32_t b_img = (uint32_t)n_tile * 128u;
+        for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
+          const Item it = decode<SPLIT>(p, t);
+          const int nt = it.nt;
+          if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(gbase + (size_t)gs * p.g_stage);
-          const uint32_t sb = p.b_res ? smem_u32(bres + ((size_t)nt * p.slabs + s) * p.b_bytes) : sa + kTerms * kAImage;
-          mma_slab<kF32>(d, sa, sa + kAImage, sb, sb + b_img, idesc, s == it.s0);
-          mma_commit(&g_empty[gs]);
-          if (++gs == p.sg) gs = 0, gph ^= 1u;
+          const uint32_t d = tmem + (uint32_t)acc * p.acc_stride;
+          for (int s = it.s0; s < it.s1; s++) {
+            if (!mbar_wait(&a_ready[gs], gph) || (!p.b_res && !mbar_wait(&g_full[gs], gph))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(gbase + (size_t)gs * p.g_stage);
+            const uint32_t sb = p.b_res ? smem_u32(bres + ((size_t)nt * p.slabs + s) * p.b_bytes) : sa + kTerms * kAImage;
+            mma_slab<kF32>(d, sa, sa + kAImage, sb, sb + b_img, idesc, s == it.s0);
+            mma_commit(&g_empty[gs]);
+            if (++gs == p.sg) gs = 0, gph ^= 1u;
+          }
+          if (!ok) break;
+          mma_commit(&acc_full[acc]);
+          if (++acc == 2) acc = 0, acc_phase ^= 1u;
         }
-        if (!ok) break;
-        mma_commit(&acc_full[acc]);
-        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+        // no MMA of this thread is in flight once `drain` completes
+        mma_commit(drain);
+        if (!mbar_wait(drain, 0)) ok = false;
       }
-      // no MMA of this thread is in flight once `drain` completes
-      mma_commit(drain);
-      if (!mbar_wait(drain, 0)) ok = false;
-    }
+  }
   } else if (warp < kEpiWarp0) {
     // ------------------------------------------------------- depthwise
+    reg_alloc<kXfRegs>();
     const int grp = (warp - kXfWarp0) / kGroupWarps;
     const int ct = tid - (kXfWarp0 + grp * kGroupWarps) * 32;
     if (grp < p.ng) {
@@ -377,10 +398,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     }
   } else {
     // ------------------------------------------------------- epilogue
-    const int e = warp - kEpiWarp0;
+    // With two teams, team k takes the items of TMEM accumulator k (every
+    // other item of this CTA) so two items' epilogues run at once; with one,
+    // team 0 takes every item and team 1 idles.
+    reg_dealloc<kEpiRegs>();
+    const int team = (warp - kEpiWarp0) / kEpiW;
+    const int e = (warp - kEpiWarp0) % kEpiW;
     const int lane_base = (warp & 3) * 32;
-    int acc = 0;
+    const int t_first = (int)blockIdx.x + team * (int)gridDim.x, t_step = p.teams * (int)gridDim.x;
+    const int bar_id = 1 + team;
+    int acc = team;
     uint32_t acc_phase = 0;
+    // next accumulator (and parity) of this team
+    auto next_acc = [&]() {
+      if (p.teams == 2) acc_phase ^= 1u;
+      else if (++acc == 2) acc = 0, acc_phase ^= 1u;
+    };
+    float *epi_team = epi_smem + team * (kEpiBytes / 4);
     const int tw = p.tw, th = p.th, OH = p.epi.OH, OW = p.epi.OW;
     EpiArgs ea = p.epi;
     ea.bias = bias_smem;
@@ -393,10 +427,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         return ((long)it.b * OH + y) * OW + x;
       };
     };
-    if (!SPLIT && n_tile > 2 * kSliceCols) {
+    if (team >= p.teams) {
+      // this team has no items
+    } else if (!SPLIT && n_tile > 2 * kSliceCols) {
       // wide tiles: transposed stores straight from the epilogue warps
-      float *blk = epi_smem + e * 32 * kEpiStride;
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
+      float *blk = epi_team + e * 32 * kEpiStride;
+      for (int t = t_first; t < p.total && ok; t += t_step) {
         const Item it = decode<SPLIT>(p, t);
         uint64_t *full = &acc_full[acc];
         const uint32_t ph = acc_phase;
@@ -412,16 +448,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+        next_acc();
       }
     } else if (!SPLIT) {
       // tiles of up to 32 columns: TMA-store epilogue, 16-column slices of the
-      // patch go out as 4-D boxes (tensor edges clipped by TMA); the four warps
-      // meet at named barrier 1.
-      uint8_t *bufs = reinterpret_cast<uint8_t *>(epi_smem);
-      const bool elected = warp == kEpiWarp0 && lane == 0;
+      // patch go out as 4-D boxes (tensor edges clipped by TMA); the team's
+      // four warps meet at named barrier 1 + team.
+      uint8_t *bufs = reinterpret_cast<uint8_t *>(epi_team);
+      const bool elected = e == 0 && lane == 0;
       uint32_t slice = 0;
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
+      for (int t = t_first; t < p.total && ok; t += t_step) {
         const Item it = decode<SPLIT>(p, t);
         uint64_t *full = &acc_full[acc];
         const uint32_t ph = acc_phase;
@@ -431,9 +467,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         const int n0 = it.nt * n_tile;
         if (!epilogue_tma<T>(
                 ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), row, n_tile, n0, m, bufs, slice,
-                elected, 1, kEpiW * 32,
-                [full, ph]() {
-                  const bool w = bar_and(1, kEpiW * 32, mbar_wait(full, ph));
+                elected, bar_id, kEpiW * 32,
+                [full, ph, bar_id]() {
+                  const bool w = bar_and(bar_id, kEpiW * 32, mbar_wait(full, ph));
                   tc_fence_after();
                   return w;
                 },
@@ -446,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
           ok = false;
           break;
         }
-        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+        next_acc();
       }
       if (elected) bulk_wait_all();  // the output is written before the CTA leaves
     } else {
@@ -455,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
       // The four epilogue warps agree on every outcome through named barrier 1,
       // so none of them is left waiting at it.
       const size_t tile_elems = (size_t)kTileM * n_tile;
-      for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
+      for (int t = t_first; t < p.total && ok; t += t_step) {
         const Item it = decode<SPLIT>(p, t);
         const bool w = bar_and(1, kEpiW * 32, mbar_wait(&acc_full[acc], acc_phase));
         tc_fence_after();
@@ -469,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+        next_acc();
         __threadfence();
         bar_named(1, kEpiW * 32);
         if (warp == kEpiWarp0 && lane == 0) *last_flag = atomicAdd(&p.cnt[it.id], 1) == p.ksplit - 1 ? 1u : 0u;
