@@ -826,7 +826,10 @@ __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh
     for (int k = 0; k < 9; k++) {
       const float spatial = spatial_k[k];
       const float dl = (here - there[k]) * inv;
-      const float wgt = spatial * expf(-dl * dl * 0.5f);
+      // exp on the hardware exp2 (within the accuracy WGSL gives the
+      // reference shader's exp; the full-range expf sequence was most of
+      // this kernel's instructions)
+      const float wgt = spatial * __expf(-dl * dl * 0.5f);
       weighted = fmaf(disp[k], wgt, weighted);
       total_w += wgt;
     }

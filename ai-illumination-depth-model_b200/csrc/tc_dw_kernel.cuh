@@ -71,14 +71,6 @@ static_assert(128 * kProducerRegs + 256 * kXfRegs + 256 * kEpiRegs <= kThreads *
 constexpr uint32_t kEpiBytes = 2 * kSliceBytes > kEpiW * 32 * kEpiStride * 4 ? 2 * kSliceBytes
                                                                              : kEpiW * 32 * kEpiStride * 4;
 
-template <uint32_t N>
-__device__ __forceinline__ void reg_alloc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <uint32_t N>
-__device__ __forceinline__ void reg_dealloc() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
 
 struct Params {
   const uint8_t *wimg;   // pointwise images [n tile][slab], b_bytes each
