@@ -73,6 +73,12 @@ struct GemmOp {
   size_t ws_bytes = 0;
   int *ws_cnt = nullptr;
   int ws_cnt_n = 0;
+  // Optional depth head on the op's output (dw->pw on the tensor engine):
+  // head_dst[m] = sigmoid(head_b + sum_n dst[m][n] * head_w[n]), folded into
+  // the epilogue when the launch allows it, else a separate head launch.
+  const float *head_w = nullptr;
+  float head_b = 0.0f;
+  float *head_dst = nullptr;
 };
 
 cudaError_t gemm(int T, const GemmOp &op, cudaStream_t st);

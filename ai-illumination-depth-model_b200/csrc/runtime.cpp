@@ -143,6 +143,7 @@ struct illumina_model {
   float *d_splitk = nullptr;         // split-K partial tiles of the tensor dw->pw kernel
   int *d_splitk_cnt = nullptr;       // its per-item arrival counters (zero between launches)
   int stem_fused_op = -1;            // conv op folded into the preprocess launch, or -1
+  int head_fused_op = -1;            // head op folded into the preceding dw->pw launch, or -1
   bool stem_writes_input = true;     // the folded launch still writes the network input
 
   void *tensor(const std::string &name) {
@@ -244,6 +245,20 @@ void plan_stem_fusion(illumina_model &m) {
   m.stem_writes_input = m.opts.keep_intermediates != 0 || tensor_live_at_end(m, ops[0].out);
 }
 
+// Folds the head into the dw->pw op right before it when that op produces the
+// head's input (tensor engine only; the op's output is still written, and
+// tc_dw launches the head itself when its tiling cannot fold it).
+void plan_head_fusion(illumina_model &m) {
+  m.head_fused_op = -1;
+  if (m.engine != ILLUMINA_ENGINE_TENSOR) return;
+  const auto &ops = m.arch.ops;
+  for (size_t i = 1; i < ops.size(); i++)
+    if (ops[i].kind == OpKind::Head && ops[i - 1].kind == OpKind::Dwpw && ops[i].in == ops[i - 1].out) {
+      m.head_fused_op = (int)i;
+      return;
+    }
+}
+
 // Enqueues the whole op list on m.stream. mode 0: independent frames -> disp;
 // mode 1: streaming frame with history (n == 1).
 // The node most recently added to the graph being captured on `st`.
@@ -340,6 +355,11 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
             g.dw_w = w.dw_w, g.dw_b = w.dw_b;
             g.ws = m.d_splitk, g.ws_bytes = m.d_splitk ? kSplitKBytes : 0;
             g.ws_cnt = m.d_splitk_cnt, g.ws_cnt_n = m.d_splitk_cnt ? kSplitKItems : 0;
+            if ((int)i + 1 == m.head_fused_op) {
+              // the head that reads this op's output runs in its epilogue
+              const OpWeights &hw = m.opw[i + 1];
+              g.head_w = hw.w, g.head_b = hw.head_bias, g.head_dst = (float *)m.tensor(a.ops[i + 1].out);
+            }
           } else {
             g.mode = 0;
           }
@@ -355,8 +375,10 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
         const TensorShape &si = a.shape(op.in);
         long M = (long)n * si.h * si.w;
         float *low = (float *)m.tensor(op.out);
-        cuda_check(gpu::head(m.T, m.tensor(op.in), M, si.c, w.w, w.head_bias, low, nullptr, st), "head");
-        launches++;
+        if ((int)i != m.head_fused_op) {
+          cuda_check(gpu::head(m.T, m.tensor(op.in), M, si.c, w.w, w.head_bias, low, nullptr, st), "head");
+          launches++;
+        }
         if (low_out) {
           cuda_check(cudaMemcpyAsync(low_out, low, sizeof(float) * M, cudaMemcpyDeviceToDevice, st), "depth_low copy");
           if (nodes) nodes->low = last_captured_node(st);
@@ -608,6 +630,7 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
   if (o.gemm_engine != ILLUMINA_ENGINE_TENSOR && o.gemm_engine != ILLUMINA_ENGINE_SIMT)
     throw Error(ILLUMINA_INVALID_ARG, "createDepthModel: unknown gemm engine " + std::to_string(o.gemm_engine));
   m.engine = o.gemm_engine;
+  plan_head_fusion(m);
   cuda_check(cudaMalloc(&m.d_err, sizeof(int)), "cudaMalloc error flag");
   cuda_check(cudaMemsetAsync(m.d_err, 0, sizeof(int), m.stream), "clear error flag");
   if (o.gemm_engine == ILLUMINA_ENGINE_TENSOR) {

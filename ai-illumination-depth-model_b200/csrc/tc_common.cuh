@@ -252,6 +252,11 @@ struct EpiArgs {
   // output column n at cs[r * cs_ld + n - cs_n0]; null: computed from `coarse`
   const float *cs;
   int cs_ld, cs_n0;
+  // the depth head folded into the epilogue (TMA-store path, one n tile):
+  // per pixel sigmoid(head_b + sum_n stored(n) * head_w[n]) into head_dst[m]
+  const float *head_w = nullptr;
+  float head_b = 0.0f;
+  float *head_dst = nullptr;
 };
 
 // Accumulator-independent inputs of one 16-column block for the 4 rows a
@@ -531,6 +536,12 @@ __device__ __forceinline__ void slice_put<__nv_bfloat16>(uint8_t *buf, int row, 
   }
 }
 // Residual of one row's 16 slice columns (zero where absent or past N).
+// The value a store of v as T keeps.
+template <typename T>
+__device__ __forceinline__ float stored_value(float v) {
+  return sizeof(T) == 4 ? v : __bfloat162float(__float2bfloat16_rn(v));
+}
+
 template <typename T>
 __device__ __forceinline__ void slice_res(const EpiArgs &a, long m, int n, float (&r)[kSliceCols]) {
   const T *res = reinterpret_cast<const T *>(a.res);
@@ -549,6 +560,7 @@ __device__ __forceinline__ bool epilogue_tma_body(const EpiArgs &a, uint32_t tac
   float rv[kSliceCols];
   slice_res<T>(a, m, n_base, rv);
   if (!ready()) return false;
+  float hs = a.head_b;  // folded head: the stored values in column order, as k_head sums them
   // slices go out in pairs (32 columns): one barrier pair and two stores per
   // pair, into one pair of buffers
   for (int cb = 0; cb < ncols; cb += 2 * kSliceCols) {
@@ -577,6 +589,11 @@ __device__ __forceinline__ bool epilogue_tma_body(const EpiArgs &a, uint32_t tac
       if (c + kSliceCols < ncols) slice_res<T>(a, m, n + kSliceCols, rv);  // next slice's residual in flight
 #pragma unroll
       for (int j = 0; j < kSliceCols; j++) o[j] = act_c<ACT>(o[j]);
+      if (a.head_dst) {
+#pragma unroll
+        for (int j = 0; j < kSliceCols; j++)
+          if (n + j < a.N) hs = fmaf(stored_value<T>(o[j]), __ldg(a.head_w + n + j), hs);
+      }
       if (m >= 0) slice_put<T>(buf + h * kSliceBytes, row, o);
     }
     fence_async_smem();
@@ -587,6 +604,7 @@ __device__ __forceinline__ bool epilogue_tma_body(const EpiArgs &a, uint32_t tac
     }
     slice++;
   }
+  if (a.head_dst && m >= 0) a.head_dst[m] = 1.0f / (1.0f + expf(-hs));
   return true;
 }
 

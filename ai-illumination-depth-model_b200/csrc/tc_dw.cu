@@ -280,6 +280,9 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   // epilogues run at once) when its buffers fit beside the planned rings
   p.teams = tl.ksplit == 1 && tl.smem + tcd::kEpiBytes <= kSmemBudget ? 2 : 1;
   const size_t smem = tl.smem + (p.teams - 1) * tcd::kEpiBytes;
+  // the head folds into the TMA-store epilogue when one tile holds every column
+  const bool fold_head = op.head_dst && tl.ksplit == 1 && plan.n_tiles == 1 && plan.n_tile <= 2 * tcx::kSliceCols;
+  if (fold_head) p.epi.head_w = op.head_w, p.epi.head_b = op.head_b, p.epi.head_dst = op.head_dst;
   p.halo_bytes = (uint32_t)(tl.iw * tl.ih * 128);
   p.dw_bytes = (uint32_t)((op.ks * op.ks + 1) * slab_c * 4);
   p.h_stage = (uint32_t)align_to(p.halo_bytes + p.dw_bytes, 1024);
@@ -290,11 +293,16 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.tmem_cols = 2 * p.acc_stride;
   p.bias_bytes = (uint32_t)align_to((size_t)op.N * 4, 16);
   const bool split = tl.ksplit > 1;
+  cudaError_t e;
   if (T == F32)
-    return split ? tcd::launch_all<float, true>(op.ks, op.stride, tl.P, map, map_out, p, smem, st)
-                 : tcd::launch_all<float, false>(op.ks, op.stride, tl.P, map, map_out, p, smem, st);
-  return split ? tcd::launch_all<__nv_bfloat16, true>(op.ks, op.stride, tl.P, map, map_out, p, smem, st)
-               : tcd::launch_all<__nv_bfloat16, false>(op.ks, op.stride, tl.P, map, map_out, p, smem, st);
+    e = split ? tcd::launch_all<float, true>(op.ks, op.stride, tl.P, map, map_out, p, smem, st)
+              : tcd::launch_all<float, false>(op.ks, op.stride, tl.P, map, map_out, p, smem, st);
+  else
+    e = split ? tcd::launch_all<__nv_bfloat16, true>(op.ks, op.stride, tl.P, map, map_out, p, smem, st)
+              : tcd::launch_all<__nv_bfloat16, false>(op.ks, op.stride, tl.P, map, map_out, p, smem, st);
+  if (e == cudaSuccess && op.head_dst && !fold_head)
+    e = head(T, op.dst, op.M, op.N, op.head_w, op.head_b, op.head_dst, nullptr, st);
+  return e;
 }
 
 }  // namespace gpu
