@@ -301,6 +301,90 @@ def run_reference(args, rank, world):
 # our arm
 # ---------------------------------------------------------------------------
 
+RELIGHT_W, RELIGHT_H = 1920, 1080
+RELIGHT_STEPS = (16, 6, 4, 12)  # contact, AO directions x steps (24 samples), volumetric per light (x4 = 48)
+
+
+def depth_relight_frame(model, frames, ring, stream, ev0, ev1, reps=60):
+    """Depth + relighting frame at batch 1: forward of a uniform 448 frame, its disparity
+    bilinearly upsampled to 1920x1080, shaded with 4 seeded point lights (24 AO samples,
+    16 contact steps, 12 volumetric steps per light) with the frame's RGB as albedo
+    (bilinear, i.e. upsampled), tone-mapped to 8-bit sRGB. Returns ms per frame and
+    the shading kernel's share."""
+    import torch
+    from illumina import _lib
+    from illumina import lighting as L
+    from illumina.workloads import config4_lights
+
+    lib = _lib.lib()
+    d448 = torch.empty((1, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    d1080 = torch.empty((RELIGHT_H, RELIGHT_W), dtype=torch.float32, device="cuda")
+    rgba8 = torch.empty((RELIGHT_H, RELIGHT_W, 4), dtype=torch.uint8, device="cuda")
+    lights = L.packLights(config4_lights(0, RELIGHT_W / RELIGHT_H, L.DEFAULT_SETTINGS.fovY))
+    sh = _lib.stream_handle(stream)
+
+    def upsample():
+        _lib.check(lib.illumina_resize_bilinear(d448.data_ptr(), SIZE, SIZE, d1080.data_ptr(), RELIGHT_W,
+                                                RELIGHT_H, sh))
+
+    def shade(i):
+        L.shade(d1080, RELIGHT_W, RELIGHT_H, frames[i % ring], SIZE, SIZE, lights, L.DEFAULT_SETTINGS, i,
+                RELIGHT_W, RELIGHT_H, rgba8=rgba8, steps=RELIGHT_STEPS, stream=stream)
+
+    def frame(i):
+        model.forward(frames[i % ring:i % ring + 1], disparity=d448, stream=stream)
+        upsample()
+        shade(i)
+
+    for i in range(5):
+        frame(i)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for i in range(reps):
+        frame(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    frame_ms = ev0.elapsed_time(ev1) / reps
+    ev0.record(stream)
+    for i in range(reps):
+        shade(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    shade_ms = ev0.elapsed_time(ev1) / reps
+    return {"ms_per_frame": frame_ms, "shade_ms": shade_ms, "resolution": f"{RELIGHT_W}x{RELIGHT_H}",
+            "mpix_per_s_shade": RELIGHT_W * RELIGHT_H / shade_ms / 1e3,
+            "steps": {"contact": RELIGHT_STEPS[0], "ao_samples": RELIGHT_STEPS[1] * RELIGHT_STEPS[2],
+                      "volumetric_per_light": RELIGHT_STEPS[3], "lights": 4},
+            "input": "uniform [0,1] 448 frame, batch 1; albedo = the frame's RGB (bilinear)"}
+
+
+def bf16_throughput(local_rank, stream, ev0, ev1, batch=256, reps=5):
+    """BF16 weights and activations (fp32 accumulation on tcgen05) at batch 256 on uniform
+    frames: frames/s on device-resident inputs."""
+    import torch
+    import illumina
+    from illumina import _lib
+
+    arch = illumina.buildArchitecture(SIZE)
+    m = illumina.createDepthModel(arch, synthSeed=0, maxBatch=batch, precision="bf16", device=local_rank)
+    frames = torch.empty((batch, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().illumina_generate_frames(0, 0, batch, SIZE, frames.data_ptr(), None))
+    disp = torch.empty((batch, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        m.forward(frames, disparity=disp, stream=stream)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(reps):
+        m.forward(frames, disparity=disp, stream=stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / reps
+    m.destroy()
+    del frames, disp
+    return {"frames_per_s": batch * 1000.0 / ms, "ms_per_step": ms, "batch": batch,
+            "input": "uniform [0,1] frames", "precision": "bf16 weights+activations, fp32 accumulate"}
+
+
 def run_ours(args, rank, local_rank, world):
     import numpy as np
     import torch
@@ -416,7 +500,10 @@ def run_ours(args, rank, local_rank, world):
         ev1.record(stream)
         torch.cuda.synchronize()
         extras["batch1_us_per_frame"] = 1000.0 * ev0.elapsed_time(ev1) / reps
+        extras["depth_relight_1080p"] = depth_relight_frame(model, b1_frames, ring, stream, ev0, ev1)
         del b1_frames
+    if rank == 0 and not args.no_extras and args.precision == "f32":
+        extras["bf16_b256"] = bf16_throughput(local_rank, stream, ev0, ev1)
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
