@@ -164,5 +164,29 @@ cudaError_t shade(const float *depth, int dw, int dh, int dch, const float *albe
                   float *hdr, uint8_t *rgba8, cudaStream_t st);
 cudaError_t resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh, cudaStream_t st);
 
+// Procedural scene and depth metrics (scene.cu). SceneParams is the scene's
+// uniform block (camera.xyz + time, look-at.xyz + tan(fovY/2), aspect, far,
+// key-light azimuth, variant); one launch renders up to kSceneBatch frames
+// whose uniforms travel in the kernel's parameter block.
+struct SceneParams {
+  float camera[4], focus[4], options[4];
+};
+constexpr int kSceneBatch = 64;
+struct SceneBatch {
+  int first;
+  SceneParams frames[kSceneBatch];
+};
+struct DepthMetrics {
+  long long samples;
+  double abs_rel, rmse, delta1, delta2, delta3, scale, shift;
+};
+// n frames of w x h: rgb (n x 3 x h x w, nullable), rgba8 (n x h x w x 4,
+// nullable), truth (n x h x w x 2 float: depth, hit; nullable). params: host array of n.
+cudaError_t scene_render(const SceneParams *params, int n, int w, int h, float *rgb, uint8_t *rgba8, float *truth,
+                         cudaStream_t st);
+// pred: n maps of `plane` texels of pred_ch floats (channel 0 read); truth: n x plane x 2; out: n (device).
+cudaError_t evaluate_depth(const float *pred, int pred_ch, const float *truth, int n, long plane, DepthMetrics *out,
+                           cudaStream_t st);
+
 }  // namespace gpu
 }  // namespace illumina

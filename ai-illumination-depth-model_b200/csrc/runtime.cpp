@@ -1172,6 +1172,53 @@ illumina_status illumina_resize_bilinear(const float *src, int sw, int sh, float
   ILL_CATCH
 }
 
+// ---- procedural scene and depth metrics ------------------------------------------
+
+static_assert(sizeof(illumina_scene_params) == sizeof(gpu::SceneParams), "scene params layout");
+static_assert(sizeof(illumina_depth_metrics) == sizeof(gpu::DepthMetrics), "depth metrics layout");
+
+void illumina_scene_params_initial(illumina_scene_params *p) {
+  if (!p) return;
+  const float tan_half = (float)std::tan((58.0 * M_PI) / 180.0 / 2.0);
+  const float v[12] = {0.0f, 0.35f, 0.6f, 0.0f, 0.0f, -0.15f, -3.0f, tan_half, 1.0f, 30.0f, 0.9f, 0.0f};
+  std::memcpy(p, v, sizeof(v));
+}
+
+void illumina_scene_params_update(illumina_scene_params *p, double time, int orbit) {
+  if (!p) return;
+  const double angle = orbit ? std::sin(time * 0.18) * 0.5 : 0.0;
+  const double height = 0.35 + (orbit ? std::sin(time * 0.11) * 0.12 : 0.0);
+  const float v[12] = {(float)(std::sin(angle) * 1.4), (float)height, (float)(0.6 + std::cos(angle) * 0.3),
+                       (float)time, 0.0f, -0.15f, -3.0f, (float)std::tan((58.0 * M_PI) / 180.0 / 2.0),
+                       1.0f, 30.0f, (float)(0.9 + time * 0.03), 0.0f};
+  std::memcpy(p, v, sizeof(v));
+}
+
+illumina_status illumina_scene_render(const illumina_scene_params *params, int n, int width, int height, float *rgb,
+                                      uint8_t *rgba8, float *truth, void *stream) {
+  ILL_TRY
+  require(n >= 0 && width > 0 && height > 0, "scene_render: bad size");
+  require(n == 0 || params, "scene_render: params is null");
+  cuda_check(gpu::scene_render(reinterpret_cast<const gpu::SceneParams *>(params), n, width, height, rgb, rgba8,
+                               truth, (cudaStream_t)stream),
+             "scene_render");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_evaluate_depth(const float *pred, int pred_channels, const float *truth, int n, int width,
+                                        int height, illumina_depth_metrics *out, void *stream) {
+  ILL_TRY
+  require(n >= 0 && width > 0 && height > 0, "evaluate_depth: bad size");
+  require(pred_channels >= 1, "evaluate_depth: pred_channels must be >= 1");
+  require(n == 0 || (pred && truth && out), "evaluate_depth: null pointer");
+  cuda_check(gpu::evaluate_depth(pred, pred_channels, truth, n, (long)width * height,
+                                 reinterpret_cast<gpu::DepthMetrics *>(out), (cudaStream_t)stream),
+             "evaluate_depth");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
 // ---- workloads -------------------------------------------------------------------
 
 illumina_status illumina_generate_frames(int kind, uint32_t seed0, int n, int size, float *out, void *stream) {

@@ -10,6 +10,7 @@ The names mirror the reference's TypeScript API surface for the hot path:
   lighting  packLights, ShadingSettings, DEFAULT_SETTINGS,
             createRenderer -> Renderer                               (src/lighting/*.ts)
   frame     renderFrame -> FrameResult                               (src/engine/frame.ts)
+  scene     createProceduralScene, renderScenes, evaluateDepth       (src/scene/procedural.ts, metrics.ts)
   ops       per-kernel entry points                                  (src/model/kernels/*.ts)
 
 Everything computes in libillumina.so (CUDA for sm_100a); there is no CPU path.
@@ -21,6 +22,8 @@ from .frame import FrameResult, renderFrame  # noqa: F401
 from .lighting import (DEFAULT_SETTINGS, MAX_LIGHTS, LightDescription, LightKind, Renderer,  # noqa: F401
                        ShadingSettings, createRenderer, packLights)
 from .runner import DepthModel, createDepthModel  # noqa: F401
+from .scene import (DepthMetrics, ProceduralScene, createProceduralScene, evaluateDepth,  # noqa: F401
+                    renderScenes, sceneParams)
 from .weights import (halfToFloat, opWeights, parseWeights, serializeWeights,  # noqa: F401
                       synthesizeWeights, totalParameters)
 

@@ -46,6 +46,16 @@ class Stats(C.Structure):
     ]
 
 
+class SceneParamsC(C.Structure):
+    _fields_ = [("camera", C.c_float * 4), ("focus", C.c_float * 4), ("options", C.c_float * 4)]
+
+
+class DepthMetricsC(C.Structure):
+    _fields_ = [("samples", C.c_longlong), ("abs_rel", C.c_double), ("rmse", C.c_double),
+                ("delta1", C.c_double), ("delta2", C.c_double), ("delta3", C.c_double),
+                ("scale", C.c_double), ("shift", C.c_double)]
+
+
 class Light(C.Structure):
     _fields_ = [("position", C.c_float * 4), ("color", C.c_float * 4), ("direction", C.c_float * 4),
                 ("params", C.c_float * 4)]
@@ -116,6 +126,10 @@ SIGNATURES = {
                             C.POINTER(ShadingSettingsC), C.c_uint32, C.POINTER(ShadeSteps), C.c_int,
                             C.c_int, _V, _V, _V]),
     "illumina_resize_bilinear": (_S, [_V, C.c_int, C.c_int, _V, C.c_int, C.c_int, _V]),
+    "illumina_scene_params_initial": (None, [C.POINTER(SceneParamsC)]),
+    "illumina_scene_params_update": (None, [C.POINTER(SceneParamsC), C.c_double, C.c_int]),
+    "illumina_scene_render": (_S, [C.POINTER(SceneParamsC), C.c_int, C.c_int, C.c_int, _V, _V, _V, _V]),
+    "illumina_evaluate_depth": (_S, [_V, C.c_int, _V, C.c_int, C.c_int, C.c_int, _V, _V]),
     "illumina_generate_frames": (_S, [C.c_int, C.c_uint32, C.c_int, C.c_int, _V, _V]),
     "illumina_checksums": (_S, [_V, C.c_int, C.c_long, _V, _V, _V]),
 }

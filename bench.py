@@ -358,6 +358,46 @@ def depth_relight_frame(model, frames, ring, stream, ev0, ev1, reps=60):
             "input": "uniform [0,1] 448 frame, batch 1; albedo = the frame's RGB (bilinear)"}
 
 
+def scene_and_metrics(model, stream, ev0, ev1, batch=64, reps=5):
+    """Procedural-scene ground truth at 448 (RGB + exact depth for `batch` frames per
+    launch, the orbiting camera of ProceduralScene.update) and evaluateDepth of the
+    network's disparity against it, all on the device."""
+    import torch
+    from illumina import _lib, renderScenes, sceneParams
+
+    lib = _lib.lib()
+    params = [sceneParams(0.25 * i, True) for i in range(batch)]
+    rgb = torch.empty((batch, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    truth = torch.empty((batch, SIZE, SIZE, 2), dtype=torch.float32, device="cuda")
+    disp = torch.empty((batch, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    out = torch.empty((batch, 64), dtype=torch.uint8, device="cuda")
+
+    def render():
+        renderScenes(params, SIZE, SIZE, rgb=rgb, truth=truth, stream=stream)
+
+    def metrics():
+        _lib.check(lib.illumina_evaluate_depth(disp.data_ptr(), 1, truth.data_ptr(), batch, SIZE, SIZE,
+                                               out.data_ptr(), _lib.stream_handle(stream)))
+
+    render()
+    model.forward(rgb, disparity=disp, stream=stream)
+    for _ in range(3):
+        render()
+        metrics()
+    torch.cuda.synchronize()
+    res = {}
+    for name, fn in (("render", render), ("metrics", metrics)):
+        ev0.record(stream)
+        for _ in range(reps):
+            fn()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        res[name] = ev0.elapsed_time(ev1) / reps
+    return {"render_frames_per_s": batch * 1000.0 / res["render"], "render_ms": res["render"],
+            "metrics_ms": res["metrics"], "metrics_gb_per_s": batch * SIZE * SIZE * 12 / res["metrics"] / 1e6,
+            "batch": batch, "outputs": "rgb 3x448x448 f32 + truth 448x448x2 f32 per frame"}
+
+
 def bf16_throughput(local_rank, stream, ev0, ev1, batch=256, reps=5):
     """BF16 weights and activations (fp32 accumulation on tcgen05) at batch 256 on uniform
     frames: frames/s on device-resident inputs."""
@@ -501,6 +541,7 @@ def run_ours(args, rank, local_rank, world):
         torch.cuda.synchronize()
         extras["batch1_us_per_frame"] = 1000.0 * ev0.elapsed_time(ev1) / reps
         extras["depth_relight_1080p"] = depth_relight_frame(model, b1_frames, ring, stream, ev0, ev1)
+        extras["scene_448"] = scene_and_metrics(model, stream, ev0, ev1)
         del b1_frames
     if rank == 0 and not args.no_extras and args.precision == "f32":
         extras["bf16_b256"] = bf16_throughput(local_rank, stream, ev0, ev1)

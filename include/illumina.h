@@ -336,6 +336,57 @@ illumina_status illumina_resize_bilinear(const float *src, int sw, int sh, float
                                          void *stream);
 
 /* ---------------------------------------------------------------------------
+ * Procedural scene and depth metrics (src/scene/)
+ * ------------------------------------------------------------------------- */
+
+/* SceneParams (procedural.ts:23-30): camera = xyz position + time in seconds,
+ * focus = xyz look-at point + tan(fovY/2), options = aspect, far plane,
+ * key-light azimuth, scene variant. */
+typedef struct illumina_scene_params {
+  float camera[4];
+  float focus[4];
+  float options[4];
+} illumina_scene_params;
+
+/* The uniforms createProceduralScene starts with (procedural.ts:295-299). */
+void illumina_scene_params_initial(illumina_scene_params *p);
+
+/* ProceduralScene.update(time, orbit) (procedural.ts:310-318): the camera
+ * orbit and the key light's drift, evaluated in double and stored as float. */
+void illumina_scene_params_update(illumina_scene_params *p, double time_seconds, int orbit);
+
+/* The ray-marched SDF scene (sceneVertex/sceneFragment, procedural.ts:177-273)
+ * for n frames of width x height, frame i with params[i] (host array). It
+ * replaces the record() draw into an rgba8unorm colour target and an
+ * rgba16float truth target with device buffers, each nullable:
+ *   rgb   n x 3 x height x width float32: the 8-bit colour as value/255, the
+ *         planar frame layout illumina_forward takes (what sampling the
+ *         rgba8unorm source texture yields);
+ *   rgba8 n x height x width x 4 bytes: the colour target itself;
+ *   truth n x height x width x 2 float32: (distance along the view axis, hit
+ *         mask), the truth target's x and y, kept in float32.
+ * Pixel (x, y), y down, is the fragment at uv = ((x+0.5)/width, (y+0.5)/height). */
+illumina_status illumina_scene_render(const illumina_scene_params *params, int n, int width, int height,
+                                      float *rgb, uint8_t *rgba8, float *truth, void *stream);
+
+/* DepthMetrics (metrics.ts:17-32). */
+typedef struct illumina_depth_metrics {
+  long long samples;
+  double abs_rel, rmse, delta1, delta2, delta3, scale, shift;
+} illumina_depth_metrics;
+
+/* evaluateDepth (metrics.ts:66-161) for n frames on the device, without the
+ * reference's texture readback: predicted disparity is channel 0 of
+ * pred_channels-float texels (1 for illumina_forward's disparity, 4 for a
+ * depth slot), truth is the scene's (depth, hit) pairs, both width x height per
+ * frame. Least-squares scale/shift in disparity space over pixels with hit >=
+ * 0.5 and 0.05 < depth <= 25, then AbsRel, RMSE and delta1..3 of the aligned
+ * depth, in double; fewer than 64 valid pixels gives NaN errors and zero
+ * deltas, as the reference does. out: n structs, device memory. */
+illumina_status illumina_evaluate_depth(const float *pred, int pred_channels, const float *truth, int n, int width,
+                                        int height, illumina_depth_metrics *out, void *stream);
+
+/* ---------------------------------------------------------------------------
  * Synthetic workloads and checksums
  * ------------------------------------------------------------------------- */
 
