@@ -14,9 +14,11 @@
 // k_metrics is evaluateDepth (src/scene/metrics.ts:66-161) on device maps: the
 // least-squares (scale, shift) in disparity space over valid pixels (hit,
 // 0.05 < depth <= 25), then AbsRel, RMSE and delta1..3 of the aligned depth,
-// all in double. One CTA per frame reads the frame twice (the second pass from
-// L2) and reduces in a fixed order, so results are deterministic; they differ
-// from the reference's sequential sums only in double rounding.
+// all in double. A cluster of 8 CTAs per frame reads the frame twice (the
+// second pass from L2) and reduces in a fixed order through distributed shared
+// memory, so results are deterministic; they differ from the reference's
+// sequential sums only in double rounding.
+#include <cooperative_groups.h>
 #include <cstdint>
 
 #include "kernels.h"
@@ -205,6 +207,7 @@ __global__ void __launch_bounds__(128) k_scene(SceneBatch batch, int w, int h, f
 // ---- metrics -----------------------------------------------------------------------
 
 constexpr int kMetricThreads = 512;
+constexpr int kMetricCluster = 8;
 
 // Block-wide sum in a fixed order: warp butterflies, then warp 0 over the warp sums.
 template <typename T>
@@ -228,53 +231,102 @@ __device__ __forceinline__ T block_sum(T v, T *smem) {
 
 __device__ __forceinline__ bool valid_truth(float2 tr) { return !(tr.y < 0.5f) && tr.x > 0.05f && !(tr.x > 25.0f); }
 
-__global__ void __launch_bounds__(kMetricThreads) k_metrics(const float *__restrict__ pred, int pred_ch,
-                                                           const float2 *__restrict__ truth, long plane,
-                                                           DepthMetrics *__restrict__ out) {
+// Per-CTA partial sums, read by the cluster's rank-0 CTA through distributed
+// shared memory.
+struct FitPart {
+  double sxx, sx, sxy, sy;
+  long long n;
+};
+struct ErrPart {
+  double abs_rel, sq;
+  long long d1, d2, d3, counted;
+};
+
+// One frame per cluster of kMetricCluster CTAs: CTA r reduces the r-th chunk of
+// the frame's pixels, rank 0 combines the chunks' partials in rank order (so
+// the result is independent of scheduling), solves the fit and publishes it to
+// the cluster for the second pass. Every CTA stays resident until the last
+// remote read of its shared memory (the trailing cluster barriers).
+__global__ void __cluster_dims__(kMetricCluster, 1, 1) __launch_bounds__(kMetricThreads)
+    k_metrics(const float *__restrict__ pred, int pred_ch, const float2 *__restrict__ truth, long plane,
+              DepthMetrics *__restrict__ out) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   __shared__ double sd[32];
   __shared__ long long sl[32];
-  const long f = blockIdx.x;
+  __shared__ FitPart fit_part;
+  __shared__ ErrPart err_part;
+  __shared__ double fit[2];
+  __shared__ long long fit_n;
+  const unsigned rank = cluster.block_rank();
+  const long f = blockIdx.x / kMetricCluster;
   const float *pf = pred + f * plane * pred_ch;
   const float2 *tf = truth + f * plane;
+  const long chunk = (plane + kMetricCluster - 1) / kMetricCluster;
+  const long begin = (long)rank * chunk, end = begin + chunk < plane ? begin + chunk : plane;
 
   long long n = 0;
   double sxx = 0, sx = 0, sxy = 0, sy = 0;
-  for (long i = threadIdx.x; i < plane; i += blockDim.x) {
+#pragma unroll 4
+  for (long i = begin + threadIdx.x; i < end; i += kMetricThreads) {
     const float2 tr = tf[i];
-    if (!valid_truth(tr)) continue;
-    const double xv = (double)pf[i * pred_ch], yv = 1.0 / (double)tr.x;
-    sxx += xv * xv;
-    sx += xv;
-    sxy += xv * yv;
-    sy += yv;
-    n++;
+    const float pv = pf[i * pred_ch];
+    if (valid_truth(tr)) {
+      const double xv = (double)pv, yv = 1.0 / (double)tr.x;
+      sxx += xv * xv;
+      sx += xv;
+      sxy += xv * yv;
+      sy += yv;
+      n++;
+    }
   }
   n = block_sum<long long>(n, sl);
   sxx = block_sum<double>(sxx, sd);
   sx = block_sum<double>(sx, sd);
   sxy = block_sum<double>(sxy, sd);
   sy = block_sum<double>(sy, sd);
-  DepthMetrics r;
-  if (n < 64) {
-    if (threadIdx.x == 0) {
-      r.samples = n;
+  if (threadIdx.x == 0) fit_part = {sxx, sx, sxy, sy, n};
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    FitPart a = {0, 0, 0, 0, 0};
+    for (unsigned r = 0; r < kMetricCluster; r++) {
+      const FitPart *p = cluster.map_shared_rank(&fit_part, r);
+      a.sxx += p->sxx;
+      a.sx += p->sx;
+      a.sxy += p->sxy;
+      a.sy += p->sy;
+      a.n += p->n;
+    }
+    const double dn = (double)a.n;
+    const double det = a.sxx * dn - a.sx * a.sx;
+    fit[0] = fabs(det) > 1e-12 ? (dn * a.sxy - a.sx * a.sy) / det : 1.0;
+    fit[1] = fabs(det) > 1e-12 ? (a.sxx * a.sy - a.sx * a.sxy) / det : 0.0;
+    fit_n = a.n;
+  }
+  cluster.sync();
+  const double *fit0 = cluster.map_shared_rank(&fit[0], 0);
+  const double scale = fit0[0], shift = fit0[1];
+  const long long total = *cluster.map_shared_rank(&fit_n, 0);
+  cluster.sync();  // rank 0's fit stays readable until every CTA has it
+  if (total < 64) {
+    if (rank == 0 && threadIdx.x == 0) {
+      DepthMetrics r;
+      r.samples = total;
       r.abs_rel = r.rmse = r.scale = r.shift = __longlong_as_double(0x7ff8000000000000ll);
       r.delta1 = r.delta2 = r.delta3 = 0.0;
       out[f] = r;
     }
     return;
   }
-  const double dn = (double)n;
-  const double det = sxx * dn - sx * sx;
-  const double scale = fabs(det) > 1e-12 ? (dn * sxy - sx * sy) / det : 1.0;
-  const double shift = fabs(det) > 1e-12 ? (sxx * sy - sx * sxy) / det : 0.0;
 
   double abs_rel = 0, sq = 0;
   long long d1 = 0, d2 = 0, d3 = 0, counted = 0;
-  for (long i = threadIdx.x; i < plane; i += blockDim.x) {
+#pragma unroll 4
+  for (long i = begin + threadIdx.x; i < end; i += kMetricThreads) {
     const float2 tr = tf[i];
+    const float pv = pf[i * pred_ch];
     if (!valid_truth(tr)) continue;
-    const double disparity = scale * (double)pf[i * pred_ch] + shift;
+    const double disparity = scale * (double)pv + shift;
     if (!(disparity > 1e-4)) continue;
     const double zhat = 1.0 / disparity, z = (double)tr.x;
     abs_rel += fabs(zhat - z) / z;
@@ -291,18 +343,32 @@ __global__ void __launch_bounds__(kMetricThreads) k_metrics(const float *__restr
   d2 = block_sum<long long>(d2, sl);
   d3 = block_sum<long long>(d3, sl);
   counted = block_sum<long long>(counted, sl);
-  if (threadIdx.x == 0) {
-    const double denom = counted > 1 ? (double)counted : 1.0;
-    r.samples = counted;
-    r.abs_rel = abs_rel / denom;
-    r.rmse = sqrt(sq / denom);
-    r.delta1 = (double)d1 / denom;
-    r.delta2 = (double)d2 / denom;
-    r.delta3 = (double)d3 / denom;
+  if (threadIdx.x == 0) err_part = {abs_rel, sq, d1, d2, d3, counted};
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    ErrPart a = {0, 0, 0, 0, 0, 0};
+    for (unsigned r = 0; r < kMetricCluster; r++) {
+      const ErrPart *p = cluster.map_shared_rank(&err_part, r);
+      a.abs_rel += p->abs_rel;
+      a.sq += p->sq;
+      a.d1 += p->d1;
+      a.d2 += p->d2;
+      a.d3 += p->d3;
+      a.counted += p->counted;
+    }
+    const double denom = a.counted > 1 ? (double)a.counted : 1.0;
+    DepthMetrics r;
+    r.samples = a.counted;
+    r.abs_rel = a.abs_rel / denom;
+    r.rmse = sqrt(a.sq / denom);
+    r.delta1 = (double)a.d1 / denom;
+    r.delta2 = (double)a.d2 / denom;
+    r.delta3 = (double)a.d3 / denom;
     r.scale = scale;
     r.shift = shift;
     out[f] = r;
   }
+  cluster.sync();  // partials stay readable until rank 0 has combined them
 }
 
 }  // namespace
@@ -327,7 +393,7 @@ cudaError_t scene_render(const SceneParams *params, int n, int w, int h, float *
 cudaError_t evaluate_depth(const float *pred, int pred_ch, const float *truth, int n, long plane, DepthMetrics *out,
                            cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
-  k_metrics<<<n, kMetricThreads, 0, st>>>(pred, pred_ch, reinterpret_cast<const float2 *>(truth), plane, out);
+  k_metrics<<<n * kMetricCluster, kMetricThreads, 0, st>>>(pred, pred_ch, reinterpret_cast<const float2 *>(truth), plane, out);
   return cudaGetLastError();
 }
 
