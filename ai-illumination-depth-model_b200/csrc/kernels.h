@@ -164,6 +164,11 @@ cudaError_t shade(const float *depth, int dw, int dh, int dch, const float *albe
                   float *hdr, uint8_t *rgba8, cudaStream_t st);
 cudaError_t resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh, cudaStream_t st);
 
+// 8-bit RGBA source (n x sh x sw x 4) sampled at the network's resolution with
+// the uv transform of makePreprocess -> planar float frames (n x 3 x size x size).
+cudaError_t sample_source(const uint8_t *rgba8, int n, int sw, int sh, const float uv_scale[2],
+                          const float uv_offset[2], int mirror, int size, float *frames, cudaStream_t st);
+
 // Procedural scene and depth metrics (scene.cu). SceneParams is the scene's
 // uniform block (camera.xyz + time, look-at.xyz + tan(fovY/2), aspect, far,
 // key-light azimuth, variant); one launch renders up to kSceneBatch frames

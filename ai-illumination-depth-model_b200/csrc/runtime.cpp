@@ -1172,6 +1172,34 @@ illumina_status illumina_resize_bilinear(const float *src, int sw, int sh, float
   ILL_CATCH
 }
 
+// ---- 8-bit source sampling ---------------------------------------------------------
+
+illumina_status illumina_sample_source(const uint8_t *rgba8, int n, int src_w, int src_h, const float *uv_scale,
+                                       const float *uv_offset, int mirror, int size, float *frames, void *stream) {
+  ILL_TRY
+  require(n >= 0 && n <= 65535, "sample_source: n must be in [0, 65535]");
+  require(src_w > 0 && src_h > 0 && size > 0, "sample_source: bad size");
+  require(n == 0 || (rgba8 && frames), "sample_source: null pointer");
+  require((reinterpret_cast<uintptr_t>(rgba8) & 3) == 0, "sample_source: rgba8 must be 4-byte aligned");
+  const float one[2] = {1.0f, 1.0f}, zero[2] = {0.0f, 0.0f};
+  cuda_check(gpu::sample_source(rgba8, n, src_w, src_h, uv_scale ? uv_scale : one, uv_offset ? uv_offset : zero,
+                                mirror ? 1 : 0, size, frames, (cudaStream_t)stream),
+             "sample_source");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+void illumina_crop_transform(int width, int height, float out[4]) {
+  if (!out) return;
+  if (width <= 0 || height <= 0) {
+    out[0] = 1.0f, out[1] = 1.0f, out[2] = 0.0f, out[3] = 0.0f;
+    return;
+  }
+  const double sx = width > height ? (double)height / width : 1.0;
+  const double sy = height > width ? (double)width / height : 1.0;
+  out[0] = (float)sx, out[1] = (float)sy, out[2] = (float)((1 - sx) / 2), out[3] = (float)((1 - sy) / 2);
+}
+
 // ---- procedural scene and depth metrics ------------------------------------------
 
 static_assert(sizeof(illumina_scene_params) == sizeof(gpu::SceneParams), "scene params layout");

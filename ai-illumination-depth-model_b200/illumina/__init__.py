@@ -21,7 +21,7 @@ from .arena import opInputs, planArena, validateArena  # noqa: F401
 from .frame import FrameResult, renderFrame  # noqa: F401
 from .lighting import (DEFAULT_SETTINGS, MAX_LIGHTS, LightDescription, LightKind, Renderer,  # noqa: F401
                        ShadingSettings, createRenderer, packLights)
-from .runner import DepthModel, createDepthModel  # noqa: F401
+from .runner import DepthModel, createDepthModel, cropTransform  # noqa: F401
 from .scene import (DepthMetrics, ProceduralScene, createProceduralScene, evaluateDepth,  # noqa: F401
                     renderScenes, sceneParams)
 from .weights import (halfToFloat, opWeights, parseWeights, serializeWeights,  # noqa: F401

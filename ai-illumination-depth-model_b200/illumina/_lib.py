@@ -126,6 +126,9 @@ SIGNATURES = {
                             C.POINTER(ShadingSettingsC), C.c_uint32, C.POINTER(ShadeSteps), C.c_int,
                             C.c_int, _V, _V, _V]),
     "illumina_resize_bilinear": (_S, [_V, C.c_int, C.c_int, _V, C.c_int, C.c_int, _V]),
+    "illumina_sample_source": (_S, [_V, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_float),
+                                     C.c_int, C.c_int, _V, _V]),
+    "illumina_crop_transform": (None, [C.c_int, C.c_int, C.POINTER(C.c_float)]),
     "illumina_scene_params_initial": (None, [C.POINTER(SceneParamsC)]),
     "illumina_scene_params_update": (None, [C.POINTER(SceneParamsC), C.c_double, C.c_int]),
     "illumina_scene_render": (_S, [C.POINTER(SceneParamsC), C.c_int, C.c_int, C.c_int, _V, _V, _V, _V]),

@@ -49,10 +49,12 @@ def _is_torch(x) -> bool:
 class DepthModel:
     """DepthModel (runner.ts:103-146). Create with createDepthModel."""
 
-    def __init__(self, handle: int, arch: Architecture, max_batch: int):
+    def __init__(self, handle: int, arch: Architecture, max_batch: int, uvScale=(1.0, 1.0), uvOffset=(0.0, 0.0)):
         self._h = C.c_void_p(handle)
         self.arch = arch
         self.maxBatch = max_batch
+        self.uvScale = tuple(uvScale)
+        self.uvOffset = tuple(uvOffset)
 
     # -- inference --------------------------------------------------------
     def _layout(self, frames):
@@ -85,6 +87,32 @@ class DepthModel:
         check(lib().illumina_forward(self._h, ptr(frames), n, layout, ptr(disparity), ptr(depthLow),
                                      stream_handle(stream)))
         return disparity
+
+    def sampleSource(self, rgba8, uvScale=None, uvOffset=None, mirror: bool = False, frames=None, stream=None):
+        """The source-texture read of makePreprocess (io.ts:64-118): n 8-bit RGBA
+        images [n, h, w, 4] (CUDA uint8 tensor, any size) sampled at the network
+        resolution with uv * uvScale + uvOffset (the model's createDepthModel
+        options unless given), linear filtering, clamp-to-edge. Returns the planar
+        float frames [n, 3, S, S] that forward() takes."""
+        import torch
+        if rgba8.dim() == 3:
+            rgba8 = rgba8[None]
+        if rgba8.dtype != torch.uint8 or not rgba8.is_cuda or not rgba8.is_contiguous() or rgba8.shape[-1] != 4:
+            raise ValueError("rgba8 must be a contiguous CUDA uint8 tensor [n, h, w, 4]")
+        n, h, w = rgba8.shape[0], rgba8.shape[1], rgba8.shape[2]
+        S = self.arch.inputSize
+        if frames is None:
+            frames = torch.empty((n, 3, S, S), dtype=torch.float32, device=rgba8.device)
+        sc = (C.c_float * 2)(*(uvScale if uvScale is not None else self.uvScale))
+        of = (C.c_float * 2)(*(uvOffset if uvOffset is not None else self.uvOffset))
+        check(lib().illumina_sample_source(ptr(rgba8), n, w, h, sc, of, int(bool(mirror)), S, ptr(frames),
+                                           stream_handle(stream)))
+        return frames
+
+    def forwardSource(self, rgba8, uvScale=None, uvOffset=None, mirror: bool = False, disparity=None, stream=None):
+        """forward() on 8-bit source images: sampleSource, then the hot path."""
+        frames = self.sampleSource(rgba8, uvScale, uvOffset, mirror, stream=stream)
+        return self.forward(frames, disparity=disparity, stream=stream)
 
     def record(self, frame, stream=None):
         """record (runner.ts:440-449): one streaming frame blended with the temporal history."""
@@ -169,12 +197,15 @@ def createDepthModel(arch: Architecture | None = None, weights: dict | None = No
                      decodeSrgb: bool = True, exposure: float = 1.0, device: int = 0, maxBatch: int = 1,
                      precision: str = "f32", keepIntermediates: bool = False, synthSeed: int = 1,
                      rangeSigma: float = 0.12, temporalBase: float = 0.35,
-                     temporalSensitivity: float = 3.0, engine: str = "tensor") -> DepthModel:
+                     temporalSensitivity: float = 3.0, engine: str = "tensor", uvScale=(1.0, 1.0),
+                     uvOffset=(0.0, 0.0)) -> DepthModel:
     """createDepthModel (runner.ts:160-485).
 
     Weights: a WeightMap (`weights`), or an .idm container (`idm`), else the
     seeded Kaiming fallback synthesizeWeights(arch, synthSeed) (main.ts:61).
     `engine` selects the pointwise-shaped ops' engine: "tensor" (tcgen05) or "simt".
+    `uvScale`/`uvOffset` (runner.ts:88-89) transform the source uv of sampleSource /
+    forwardSource.
     """
     arch = arch or buildArchitecture(448)
     o = ModelOptions()
@@ -204,4 +235,12 @@ def createDepthModel(arch: Architecture | None = None, weights: dict | None = No
         o.idm_len = len(idm)
     h = C.c_void_p()
     check(lib().illumina_model_create(C.byref(o), C.byref(h)))
-    return DepthModel(h.value, arch, maxBatch)
+    return DepthModel(h.value, arch, maxBatch, uvScale, uvOffset)
+
+
+def cropTransform(width: int, height: int):
+    """cropTransform (scene/blit.ts:80-86): [scaleX, scaleY, offsetX, offsetY] of the
+    largest centred square, for uvScale = out[:2], uvOffset = out[2:]."""
+    out = (C.c_float * 4)()
+    lib().illumina_crop_transform(int(width), int(height), out)
+    return list(out)

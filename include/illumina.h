@@ -335,6 +335,24 @@ illumina_status illumina_shade(const float *disparity, int dw, int dh, int dispa
 illumina_status illumina_resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh,
                                          void *stream);
 
+/* The source-texture read of makePreprocess (kernels/io.ts:64-118) for an
+ * 8-bit RGBA source of any size: n images of src_h x src_w x 4 bytes (device)
+ * are sampled at uv = ((x+0.5)/size, (y+0.5)/size) * uv_scale + uv_offset
+ * (createDepthModel's uvScale/uvOffset, runner.ts:88-89, :181-182; NULL means
+ * (1,1) and (0,0)), u mirrored first when `mirror` (the blit's mirror,
+ * scene/blit.ts:57-60), with linear filtering and clamp-to-edge
+ * (runner.ts:177), texels read as value/255. Output: n x 3 x size x size
+ * planar float frames for illumina_forward (FRAME_RGB_PLANAR), which applies
+ * the sRGB decode, exposure and normalisation. */
+illumina_status illumina_sample_source(const uint8_t *rgba8, int n, int src_w, int src_h, const float *uv_scale,
+                                       const float *uv_offset, int mirror, int size, float *frames,
+                                       void *stream);
+
+/* cropTransform (scene/blit.ts:80-86): the largest centred square of a
+ * width x height image as {scaleX, scaleY, offsetX, offsetY}, for
+ * illumina_sample_source's uv_scale = out[0..1], uv_offset = out[2..3]. */
+void illumina_crop_transform(int width, int height, float out[4]);
+
 /* ---------------------------------------------------------------------------
  * Procedural scene and depth metrics (src/scene/)
  * ------------------------------------------------------------------------- */

@@ -50,6 +50,8 @@ def declare(lib):
         "or_shade": (None, [F, C.c_int, C.c_int, F, C.c_int, C.c_int, C.POINTER(Light), C.c_int,
                             C.POINTER(ShadeParams), C.POINTER(Steps), C.c_int, C.c_int, C.c_int,
                             C.c_int, F, U8]),
+        "or_sample_source": (None, [U8, C.c_int, C.c_int, C.c_int, F, F, C.c_int, C.c_int, F]),
+        "or_crop_transform": (None, [C.c_int, C.c_int, F]),
         "or_scene_params": (None, [C.c_double, C.c_int, C.c_int, F]),
         "or_scene_render": (None, [F, C.c_int, C.c_int, F, U8, F]),
         "or_evaluate_depth": (None, [F, C.c_int, F, C.c_int, C.c_int, D]),
