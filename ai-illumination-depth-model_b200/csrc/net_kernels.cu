@@ -756,87 +756,116 @@ cudaError_t head(int T, const void *src, long M, int C, const float *w, float bi
 // (luma, 1 channel) or from linear colour (guide, gc channels).
 // Parameter list mirrored by kBilateralArgCount / kBilateralDstArg.
 //
-// One thread per 2x2 output quad: output (x, y) centres its 3x3 low-res taps
-// on (floor((x + 0.5) / 2), floor((y + 0.5) / 2)), which is the same low
-// pixel for x = 2i and 2i + 1, so the quad loads the nine disparities and
-// nine guide values once; each output pixel then runs the reference's
-// per-pixel arithmetic unchanged.
-__global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh, int lw,
-                            const float *__restrict__ luma, const float *__restrict__ guide, int gc,
-                            BilateralParams p, float *__restrict__ dst, const float *__restrict__ history,
-                            float *__restrict__ out_tex) {
+// Output (x, y) centres its 3x3 low-res taps on (floor((x + 0.5) / 2),
+// floor((y + 0.5) / 2)), the same low pixel for the four pixels of a 2x2
+// quad. A CTA covers 32 x 8 quads (64 x 16 output pixels): the (8 + 2) x
+// (32 + 2) low-res disparities and guide samples its taps read, clamped to
+// the map as the reference's taps are, are staged once in shared memory; each
+// thread then runs its quad's four pixels. Per tap the weight
+// spatial * exp(-dl^2 / 2) is one hardware exp2 of the summed log2 terms,
+// log2(spatial) - (here - there)^2 * log2(e) / (2 sigma^2): the interior
+// quads' 36 spatial terms are compile-time constants (the tap offsets are
+// +-1/4, +-3/4, +-5/4 wherever the quad is), border quads compute theirs from
+// the clamped tap positions. The normalising division is the SFU reciprocal
+// product (within WGSL's 2.5 ulp division accuracy).
+constexpr int kBilTX = 32, kBilTY = 8;
+constexpr float kLog2e = 1.44269504088896340736f;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// log2 of the spatial weight of tap (dx, dy) for quad sub-pixel `sub` of an
+// interior quad: offsets (dx - sx/2 + 1/4, dy - sy/2 + 1/4), exact in binary32.
+__host__ __device__ constexpr float bil_sp2(int sub, int k) {
+  return -(((float)(k % 3 - 1) - ((float)(sub & 1) * 0.5f - 0.25f)) *
+               ((float)(k % 3 - 1) - ((float)(sub & 1) * 0.5f - 0.25f)) +
+           ((float)(k / 3 - 1) - ((float)(sub >> 1) * 0.5f - 0.25f)) *
+               ((float)(k / 3 - 1) - ((float)(sub >> 1) * 0.5f - 0.25f))) *
+         0.5f * kLog2e;
+}
+
+__global__ void __launch_bounds__(kBilTX * kBilTY) k_bilateral(const float *__restrict__ low, int lc, int n, int lh,
+                                                             int lw, const float *__restrict__ luma,
+                                                             const float *__restrict__ guide, int gc,
+                                                             BilateralParams p, float *__restrict__ dst,
+                                                             const float *__restrict__ history,
+                                                             float *__restrict__ out_tex) {
   pdl_wait();
   pdl_trigger();
-  // Spatial weights of quads whose 3x3 low-res taps are all inside the map:
-  // for sub-pixel (sx, sy) and tap (dx, dy) the offset is (dx - sx/2 + 1/4,
-  // dy - sy/2 + 1/4) wherever the quad is, computed exactly in binary32, so
-  // the table holds the very values the per-tap expression gives.
-  __shared__ float sp_tab[36];
-  if (threadIdx.x < 36) {
-    const int sub = threadIdx.x / 9, k = threadIdx.x - sub * 9;
-    const float dxs = (float)(k % 3 - 1) - ((float)(sub & 1) * 0.5f - 0.25f);
-    const float dys = (float)(k / 3 - 1) - ((float)(sub >> 1) * 0.5f - 0.25f);
-    sp_tab[threadIdx.x] = expf(-(dxs * dxs + dys * dys) * 0.5f);
-  }
-  __syncthreads();
+  __shared__ float s_disp[kBilTY + 2][kBilTX + 2];
+  __shared__ float s_there[kBilTY + 2][kBilTX + 2];
   const int S = lh * 2, SW = lw * 2;
-  const long q = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (q >= (long)n * lh * lw) return;
-  int qi, qj, b;
-  unflatten3(q, lw, lh, qi, qj, b);
-  const bool interior = qi >= 1 && qj >= 1 && qi + 1 < lw && qj + 1 < lh;
+  const int b = blockIdx.z;
+  const int qi0 = blockIdx.x * kBilTX, qj0 = blockIdx.y * kBilTY;
   auto luma_at = [&](int gx, int gy) -> float {
-    const long g = ((long)b * S + gy) * SW + gx;
+    const int g = (b * S + gy) * SW + gx;
     if (luma) return __ldg(luma + g);
-    const float *c = guide + g * gc;
+    const float *c = guide + (long)g * gc;
     return 0.2126f * __ldg(c) + 0.7152f * __ldg(c + 1) + 0.0722f * __ldg(c + 2);
   };
+  const int tid = threadIdx.y * kBilTX + threadIdx.x;
+  for (int e = tid; e < (kBilTY + 2) * (kBilTX + 2); e += kBilTX * kBilTY) {
+    const int ey = e / (kBilTX + 2), ex = e - ey * (kBilTX + 2);
+    const int qx = min(max(qi0 + ex - 1, 0), lw - 1), qy = min(max(qj0 + ey - 1, 0), lh - 1);
+    s_disp[ey][ex] = __ldg(low + ((b * lh + qy) * lw + qx) * lc);
+    s_there[ey][ex] = luma_at(qx * 2, qy * 2);
+  }
+  __syncthreads();
+  const int qi = qi0 + threadIdx.x, qj = qj0 + threadIdx.y;
+  if (qi >= lw || qj >= lh) return;
+  const int tx = threadIdx.x, ty = threadIdx.y;
   float disp[9], there[9];
-  int tqx[9], tqy[9];
 #pragma unroll
-  for (int dy = -1; dy <= 1; dy++)
+  for (int k = 0; k < 9; k++) {
+    disp[k] = s_disp[ty + k / 3][tx + k % 3];
+    there[k] = s_there[ty + k / 3][tx + k % 3];
+  }
+  // the four guide values of the quad's own pixels (row pairs as float2 when aligned)
+  float here[4];
+  const int g0 = (b * S + 2 * qj) * SW + 2 * qi;
+  if (luma && ((reinterpret_cast<uintptr_t>(luma) & 7) == 0)) {
+    const float2 h0 = __ldg(reinterpret_cast<const float2 *>(luma + g0));
+    const float2 h1 = __ldg(reinterpret_cast<const float2 *>(luma + g0 + SW));
+    here[0] = h0.x, here[1] = h0.y, here[2] = h1.x, here[3] = h1.y;
+  } else {
 #pragma unroll
-    for (int dx = -1; dx <= 1; dx++) {
-      const int k = (dy + 1) * 3 + dx + 1;
-      const int qx = min(max(qi + dx, 0), lw - 1), qy = min(max(qj + dy, 0), lh - 1);
-      tqx[k] = qx, tqy[k] = qy;
-      disp[k] = __ldg(low + (((long)b * lh + qy) * lw + qx) * lc);
-      there[k] = luma_at(qx * 2, qy * 2);
-    }
+    for (int sub = 0; sub < 4; sub++) here[sub] = luma_at(2 * qi + (sub & 1), 2 * qj + (sub >> 1));
+  }
+  const bool interior = qi >= 1 && qj >= 1 && qi + 1 < lw && qj + 1 < lh;
   const float inv = 1.0f / fmaxf(p.range_sigma, 1e-4f);
+  const float k2 = inv * inv * (0.5f * kLog2e);
   float out[4];
 #pragma unroll
   for (int sub = 0; sub < 4; sub++) {
     const int x = 2 * qi + (sub & 1), y = 2 * qj + (sub >> 1);
-    const float here = luma_at(x, y);
-    const float cx = (x + 0.5f) * 0.5f - 0.5f, cy = (y + 0.5f) * 0.5f - 0.5f;
-    float spatial_k[9];
+    float sp2[9];
     if (interior) {
 #pragma unroll
-      for (int k = 0; k < 9; k++) spatial_k[k] = sp_tab[sub * 9 + k];
+      for (int k = 0; k < 9; k++) sp2[k] = bil_sp2(sub, k);
     } else {
+      const float cx = (x + 0.5f) * 0.5f - 0.5f, cy = (y + 0.5f) * 0.5f - 0.5f;
 #pragma unroll
       for (int k = 0; k < 9; k++) {
-        const float dxs = tqx[k] - cx, dys = tqy[k] - cy;
-        spatial_k[k] = expf(-(dxs * dxs + dys * dys) * 0.5f);
+        const float dxs = (float)min(max(qi + k % 3 - 1, 0), lw - 1) - cx;
+        const float dys = (float)min(max(qj + k / 3 - 1, 0), lh - 1) - cy;
+        sp2[k] = -(dxs * dxs + dys * dys) * (0.5f * kLog2e);
       }
     }
     float weighted = 0.0f, total_w = 0.0f;
 #pragma unroll
     for (int k = 0; k < 9; k++) {
-      const float spatial = spatial_k[k];
-      const float dl = (here - there[k]) * inv;
-      // exp on the hardware exp2 (within the accuracy WGSL gives the
-      // reference shader's exp; the full-range expf sequence was most of
-      // this kernel's instructions)
-      const float wgt = spatial * __expf(-dl * dl * 0.5f);
+      const float d = here[sub] - there[k];
+      const float wgt = ex2_approx(fmaf(-d * d, k2, sp2[k]));
       weighted = fmaf(disp[k], wgt, weighted);
       total_w += wgt;
     }
-    const float up = weighted / fmaxf(total_w, 1e-6f);
+    const float up = __fdividef(weighted, fmaxf(total_w, 1e-6f));
     float o = up;
-    const long idx = ((long)b * S + y) * SW + x;
     if (out_tex) {
+      const int idx = (b * S + y) * SW + x;
       const float4 prev = history ? reinterpret_cast<const float4 *>(history)[idx] : make_float4(0, 0, 0, 0);
       const float change = fabsf(up - prev.x);
       const float alpha =
@@ -846,19 +875,27 @@ __global__ void k_bilateral(const float *__restrict__ low, int lc, int n, int lh
     }
     out[sub] = o;
   }
-  if (dst) {  // scalar stores: callers' output pointers need only 4-byte alignment
-    const long row0 = ((long)b * S + 2 * qj) * SW + 2 * qi;
-    dst[row0] = out[0], dst[row0 + 1] = out[1];
-    dst[row0 + SW] = out[2], dst[row0 + SW + 1] = out[3];
+  if (dst) {  // paired stores when the caller's pointer allows, scalar otherwise
+    if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+      reinterpret_cast<float2 *>(dst + g0)[0] = make_float2(out[0], out[1]);
+      reinterpret_cast<float2 *>(dst + g0 + SW)[0] = make_float2(out[2], out[3]);
+    } else {
+      dst[g0] = out[0], dst[g0 + 1] = out[1];
+      dst[g0 + SW] = out[2], dst[g0 + SW + 1] = out[3];
+    }
   }
 }
+
+namespace {
+dim3 bilateral_grid(int n, int lh, int lw) { return dim3((lw + kBilTX - 1) / kBilTX, (lh + kBilTY - 1) / kBilTY, n); }
+}  // namespace
 
 cudaError_t bilateral(const float *low1, int n, int lh, int lw, const float *luma, const BilateralParams &p,
                       float *dst, const float *history, float *out_tex, cudaStream_t st) {
   long total = (long)n * lh * lw * 4;
-  if (total > kMaxIndex) return cudaErrorInvalidValue;
+  if (total > kMaxIndex || n > 65535) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
-  return launch_pdl(k_bilateral, dim3(blocks_for(total / 4, 256)), dim3(256), 0, st, low1, 1, n, lh, lw, luma,
+  return launch_pdl(k_bilateral, bilateral_grid(n, lh, lw), dim3(kBilTX, kBilTY), 0, st, low1, 1, n, lh, lw, luma,
                     (const float *)nullptr, 0, p, dst, history, out_tex);
 }
 
@@ -868,8 +905,8 @@ cudaError_t bilateral_strided(const float *low, int lh, int lw, int low_c, const
   if (total > kMaxIndex) return cudaErrorInvalidValue;
   if (total == 0) return cudaSuccess;
   BilateralParams p{range_sigma, 0.35f, 3.0f};
-  k_bilateral<<<blocks_for(total / 4, 256), 256, 0, st>>>(low, low_c, 1, lh, lw, nullptr, guide, guide_c, p, dst,
-                                                          nullptr, nullptr);
+  k_bilateral<<<bilateral_grid(1, lh, lw), dim3(kBilTX, kBilTY), 0, st>>>(low, low_c, 1, lh, lw, nullptr, guide,
+                                                                          guide_c, p, dst, nullptr, nullptr);
   return cudaGetLastError();
 }
 

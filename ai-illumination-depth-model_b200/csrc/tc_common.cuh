@@ -150,10 +150,13 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 // storage issues three TF32 cross products of the hi/lo split (3xTF32: the
 // lo x lo term, ~2^-22 of the product, is dropped), small terms first.
 template <bool F32>
+// `nk`: the slab's 32-byte K chunks that hold channels (1..4); the chunks
+// past them are zero padding of the last slab and are not multiplied.
 __device__ __forceinline__ void mma_slab(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
-                                         uint32_t idesc, bool first) {
+                                         uint32_t idesc, bool first, int nk = 4) {
 #pragma unroll
   for (int kk = 0; kk < 4; kk++) {
+    if (kk >= nk) break;
     const uint32_t ko = kk * 32;
     const uint32_t acc = (first && kk == 0) ? 0u : 1u;
     if (F32) {

@@ -118,8 +118,14 @@ DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const 
   const size_t dw_bytes = (size_t)(KS * KS + 1) * slab_c * 4;
   const size_t a_bytes = (size_t)terms * tcx::kAImage, b_bytes = (size_t)terms * w.n_tile * 128;
   const size_t res_total = (size_t)w.n_tiles * w.slabs * b_bytes;
-  const double mma = f32 ? 1000.0 + 8.0 * w.n_tile : 300.0 + 2.0 * w.n_tile;
-  const double mma_rd = f32 ? 512.0 + 4.0 * w.n_tile : 128.0 + 1.0 * w.n_tile;
+  // the last slab computes and multiplies only its 32-byte K chunks that hold
+  // channels; a one-slab op is costed at that width
+  const int nk = w.slabs == 1 ? (int)((w.K * (f32 ? 4 : 2) + 31) / 32) : 4;
+  int cgs_eff = cgs;
+  if (w.slabs == 1)
+    for (cgs_eff = 1; cgs_eff < nk * (f32 ? 2 : 4);) cgs_eff <<= 1;
+  const double mma = (f32 ? 1000.0 + 8.0 * w.n_tile : 300.0 + 2.0 * w.n_tile) * nk / 4.0;
+  const double mma_rd = (f32 ? 512.0 + 4.0 * w.n_tile : 128.0 + 1.0 * w.n_tile) * nk / 4.0;
   const double epi = (w.n_tile / 16.0) * (has_res ? 1400.0 : 700.0);
   const double G = sm_count();
   DwTiling best;
@@ -138,7 +144,7 @@ DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const 
         const double items = (double)n_frames * ((OW + tw - 1) / tw) * tiles_y * w.n_tiles;
         const size_t halo = (size_t)iw * ih * 128;
         const size_t h_stage = align_to(halo + dw_bytes, 1024);
-        const int units = th * (tw / P) * cgs;
+        const int units = th * (tw / P) * cgs_eff;
         const int rounds = (units + tcd::kGroupWarps * 32 - 1) / (tcd::kGroupWarps * 32);
         const int span = (P - 1) * S + KS;
         const double xf = 6.0 * rounds * (KS * (4.0 * P * KS + span + KS) + 40.0 * P);
@@ -275,6 +281,15 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.items = (int)items, p.ksplit = tl.ksplit, p.spk = tl.spk, p.total = (int)total;
   p.ws = op.ws, p.cnt = op.ws_cnt;
   p.tw = tl.tw, p.th = tl.th, p.iw = tl.iw, p.mid_act = op.mid_act;
+  {
+    const int k_last = op.K - (plan.slabs - 1) * slab_c;  // channels in the last slab
+    p.nk_last = (int)((k_last * elt + 31) / 32);
+    // depthwise width of the last slab: its chunks' channel groups, rounded up
+    // to a power of two so a warp's halo reads still cover every bank
+    p.cg_last = 1;
+    while (p.cg_last < p.nk_last * 8 / (int)elt) p.cg_last <<= 1;
+    if (k_last <= 0 || p.nk_last > 4) return cudaErrorInvalidValue;
+  }
   p.sh = tl.sh, p.sg = tl.sg, p.b_res = tl.b_res, p.ng = tl.ng;
   // a second epilogue team (one per TMEM accumulator, so two items'
   // epilogues run at once) when its buffers fit beside the planned rings

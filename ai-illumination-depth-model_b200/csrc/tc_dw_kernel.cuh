@@ -81,6 +81,9 @@ struct Params {
   int *cnt;   // split-K arrival counters [item], zero between launches
   int tiles_x, tiles_y, n_tiles, slabs, items, ksplit, spk, total;  // total = items * ksplit units
   int tw, th, iw, mid_act;
+  // last K slab: 32-byte K chunks holding channels (MMAs issued) and the
+  // 4-channel groups they span (depthwise computed); full slabs use 4 and 128 / 4 / sizeof(T)
+  int nk_last, cg_last;
   int sh, sg, b_res, ng;
   int teams;  // epilogue teams: 2 = one per accumulator, 1 = team 0 takes every item
   uint32_t halo_bytes, dw_bytes, h_stage, g_stage, b_bytes, acc_stride, tmem_cols, bias_bytes;
@@ -149,16 +152,18 @@ __device__ __forceinline__ void a_st(const __nv_bfloat16 *, uint8_t *A, int r, i
 // thread's index within its group of kGroupWarps warps.
 template <typename T, int KS, int S, int P, int ACT>
 __device__ __forceinline__ void depthwise_slab(const Params &p, const Item &it, const uint8_t *halo,
-                                               const float *dww, uint8_t *A, int ct) {
+                                               const float *dww, uint8_t *A, int ct, int cgn) {
   constexpr int kSlabC = 128 / (int)sizeof(T);
-  constexpr int kCG = kSlabC / 4;
   constexpr int kSpan = (P - 1) * S + KS;
   const int runs = p.tw / P;
-  const int units = p.th * runs * kCG;
+  const int units = p.th * runs * cgn;
   const int OH = p.epi.OH, OW = p.epi.OW;
+  // u / cgn as a multiply-high: with m = floor(2^32 / cgn) + 1 the quotient is
+  // exact for u * cgn < 2^32 (units <= 128 x 16 here)
+  const uint32_t cg_magic = 0xffffffffu / (uint32_t)cgn + 1u;
   for (int u = ct; u < units; u += kGroupWarps * 32) {
-    const int cg = u % kCG;
-    const int q = u / kCG;
+    const int q = (int)__umulhi((uint32_t)u, cg_magic);
+    const int cg = u - q * cgn;
     const int run = q % runs, ly = q / runs;
     const int lx0 = run * P;
     if (it.y0 + ly >= OH || it.x0 + lx0 >= OW) continue;
@@ -192,12 +197,12 @@ __device__ __forceinline__ void depthwise_slab(const Params &p, const Item &it, 
 
 template <typename T, int KS, int S, int P>
 __device__ __forceinline__ void depthwise_dispatch(const Params &p, const Item &it, const uint8_t *halo,
-                                                   const float *dww, uint8_t *A, int ct) {
+                                                   const float *dww, uint8_t *A, int ct, int cgn) {
   switch (p.mid_act) {
-    case 1: depthwise_slab<T, KS, S, P, 1>(p, it, halo, dww, A, ct); break;
-    case 2: depthwise_slab<T, KS, S, P, 2>(p, it, halo, dww, A, ct); break;
-    case 3: depthwise_slab<T, KS, S, P, 3>(p, it, halo, dww, A, ct); break;
-    default: depthwise_slab<T, KS, S, P, 0>(p, it, halo, dww, A, ct); break;
+    case 1: depthwise_slab<T, KS, S, P, 1>(p, it, halo, dww, A, ct, cgn); break;
+    case 2: depthwise_slab<T, KS, S, P, 2>(p, it, halo, dww, A, ct, cgn); break;
+    case 3: depthwise_slab<T, KS, S, P, 3>(p, it, halo, dww, A, ct, cgn); break;
+    default: depthwise_slab<T, KS, S, P, 0>(p, it, halo, dww, A, ct, cgn); break;
   }
 }
 
@@ -345,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
             tc_fence_after();
             const uint32_t sa = smem_u32(gbase + (size_t)gs * p.g_stage);
             const uint32_t sb = p.b_res ? smem_u32(bres + ((size_t)nt * p.slabs + s) * p.b_bytes) : sa + kTerms * kAImage;
-            mma_slab<kF32>(d, sa, sa + kAImage, sb, sb + b_img, idesc, s == it.s0);
+            mma_slab<kF32>(d, sa, sa + kAImage, sb, sb + b_img, idesc, s == it.s0, s == p.slabs - 1 ? p.nk_last : 4);
             mma_commit(&g_empty[gs]);
             if (++gs == p.sg) gs = 0, gph ^= 1u;
           }
@@ -378,7 +383,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
           }
           const uint8_t *hst = hbase + (size_t)hs * p.h_stage;
           depthwise_dispatch<T, KS, S, P>(p, it, hst, reinterpret_cast<const float *>(hst + p.halo_bytes),
-                                          gbase + (size_t)gs * p.g_stage, ct);
+                                          gbase + (size_t)gs * p.g_stage, ct,
+                                          s == p.slabs - 1 ? p.cg_last : 32 / (int)sizeof(T));
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
