@@ -119,6 +119,12 @@ struct illumina_model {
   size_t elt = 4;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev_join = nullptr, ev_done = nullptr;
+  // host-buffer forwards run in frame chunks: uploads on copy_in and
+  // downloads on copy_out overlap the graph of the neighbouring chunks
+  static constexpr int kMaxChunks = 16;
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t ev_in[kMaxChunks] = {}, ev_fwd[kMaxChunks] = {};
+  cudaEvent_t ev_out = nullptr;
   std::vector<float> host_weights;  // logical blob (kept for debug / re-pack)
   float *d_weights_logical = nullptr;
   float *d_weights = nullptr;
@@ -180,6 +186,13 @@ illumina_model::~illumina_model() {
   cudaFree(d_splitk_cnt);
   if (ev_join) cudaEventDestroy(ev_join);
   if (ev_done) cudaEventDestroy(ev_done);
+  for (int i = 0; i < kMaxChunks; i++) {
+    if (ev_in[i]) cudaEventDestroy(ev_in[i]);
+    if (ev_fwd[i]) cudaEventDestroy(ev_fwd[i]);
+  }
+  if (ev_out) cudaEventDestroy(ev_out);
+  if (copy_in) cudaStreamDestroy(copy_in);
+  if (copy_out) cudaStreamDestroy(copy_out);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -465,6 +478,24 @@ GraphEntry &graph_for(illumina_model &m, const GraphKey &key, const float *frame
 
 // Runs the hot path with caller pointers (host or device). Host pointers are
 // staged through the model's device buffers and make the call synchronous.
+// Chunk sizes of a host-buffer forward of n frames (returns the count, 1 =
+// no chunking). Below 32 frames one launch; below 128 two halves; else chunks
+// of 64 frames (more for very large batches) with the ends tapered (16, 48, 64, ..., 48, 16) so the first
+// upload and the last download, which nothing overlaps, are short.
+int host_chunks(int n, int *sizes) {
+  if (n < 32) return sizes[0] = n, 1;
+  if (n < 128) return sizes[0] = (n + 1) / 2, sizes[1] = n - sizes[0], 2;
+  constexpr int kMid = illumina_model::kMaxChunks - 4;
+  int k = 0, rem = n;
+  sizes[k++] = 16, sizes[k++] = 48, rem -= 64;
+  // middle chunks of 64 frames, larger (multiples of 16) when 64 would need too many
+  const int mid = std::max(64, ((rem - 64 + kMid - 1) / kMid + 15) / 16 * 16);
+  while (rem > mid + 48 && k < illumina_model::kMaxChunks - 2) sizes[k++] = mid, rem -= mid;
+  if (rem > 32) sizes[k++] = rem - 16, sizes[k++] = 16;
+  else sizes[k++] = rem;
+  return k;
+}
+
 void run_forward(illumina_model &m, const float *frames, int n, int layout, float *disp, float *low,
                  cudaStream_t caller, int mode) {
   if (n < 1 || n > m.opts.max_batch)
@@ -484,6 +515,53 @@ void run_forward(illumina_model &m, const float *frames, int n, int layout, floa
 
   cuda_check(cudaEventRecord(m.ev_join, caller), "event record");
   cuda_check(cudaStreamWaitEvent(m.stream, m.ev_join, 0), "stream wait");
+
+  // Host buffers, whole batches: frame chunks, each uploaded on copy_in, run
+  // through the (chunk-sized) graph on the model stream and downloaded on
+  // copy_out, so PCIe traffic in both directions overlaps the neighbouring
+  // chunks' compute. The results are the same as one launch per chunk:
+  // frames are independent.
+  int sizes[illumina_model::kMaxChunks], chunks = host_chunks(n, sizes);
+  if (mode == 0 && (host_in || host_disp) && !low && chunks > 1) {
+    cuda_check(cudaStreamWaitEvent(m.copy_in, m.ev_join, 0), "stream wait");
+    cuda_check(cudaStreamWaitEvent(m.copy_out, m.ev_join, 0), "stream wait");
+    // every upload first (a pageable download blocks the host until its chunk
+    // is done; the uploads are queued by then), then graphs and downloads
+    long starts[illumina_model::kMaxChunks];
+    for (int k = 0, f = 0; k < chunks; f += sizes[k], k++) starts[k] = f;
+    if (host_in)
+      for (int k = 0; k < chunks; k++) {
+        const long f0 = starts[k];
+        const int nk = sizes[k];
+        cuda_check(cudaMemcpyAsync(m.d_stage_in + f0 * frame_floats, frames + f0 * frame_floats,
+                                   sizeof(float) * nk * frame_floats, cudaMemcpyHostToDevice, m.copy_in),
+                   "frames H2D");
+        cuda_check(cudaEventRecord(m.ev_in[k], m.copy_in), "event record");
+      }
+    for (int k = 0; k < chunks; k++) {
+      const long f0 = starts[k];
+      const int nk = sizes[k];
+      const float *f_dev = (host_in ? m.d_stage_in : frames) + f0 * frame_floats;
+      if (host_in) cuda_check(cudaStreamWaitEvent(m.stream, m.ev_in[k], 0), "stream wait");
+      float *d_disp = (host_disp || !disp ? m.d_stage_out : disp) + f0 * disp_floats;
+      GraphKey key{nk, layout, 0, 0, nullptr, nullptr};
+      GraphEntry &g = graph_for(m, key, f_dev, d_disp, nullptr, nullptr, nullptr);
+      cuda_check(cudaGraphLaunch(g.exec, m.stream), "graph launch");
+      if (host_disp) {
+        cuda_check(cudaEventRecord(m.ev_fwd[k], m.stream), "event record");
+        cuda_check(cudaStreamWaitEvent(m.copy_out, m.ev_fwd[k], 0), "stream wait");
+        cuda_check(cudaMemcpyAsync(disp + f0 * disp_floats, d_disp, sizeof(float) * nk * disp_floats,
+                                   cudaMemcpyDeviceToHost, m.copy_out),
+                   "disparity D2H");
+      }
+    }
+    cuda_check(cudaEventRecord(m.ev_out, m.copy_out), "event record");
+    cuda_check(cudaStreamWaitEvent(m.stream, m.ev_out, 0), "stream wait");
+    cuda_check(cudaEventRecord(m.ev_done, m.stream), "event record");
+    cuda_check(cudaStreamWaitEvent(caller, m.ev_done, 0), "caller wait");
+    cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+    return;
+  }
 
   const float *f_dev = frames;
   if (host_in) {
@@ -567,6 +645,13 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
   cuda_check(cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking), "stream create");
   cuda_check(cudaEventCreateWithFlags(&m.ev_join, cudaEventDisableTiming), "event create");
   cuda_check(cudaEventCreateWithFlags(&m.ev_done, cudaEventDisableTiming), "event create");
+  cuda_check(cudaStreamCreateWithFlags(&m.copy_in, cudaStreamNonBlocking), "stream create");
+  cuda_check(cudaStreamCreateWithFlags(&m.copy_out, cudaStreamNonBlocking), "stream create");
+  for (int i = 0; i < illumina_model::kMaxChunks; i++) {
+    cuda_check(cudaEventCreateWithFlags(&m.ev_in[i], cudaEventDisableTiming), "event create");
+    cuda_check(cudaEventCreateWithFlags(&m.ev_fwd[i], cudaEventDisableTiming), "event create");
+  }
+  cuda_check(cudaEventCreateWithFlags(&m.ev_out, cudaEventDisableTiming), "event create");
 
   // Upload the logical blob, then repack per op on the device.
   cuda_check(cudaMalloc(&m.d_weights_logical, count * 4), "cudaMalloc weights");
