@@ -342,22 +342,24 @@ cudaError_t conv(int T, const void *src, int n, int H, int W, int Cin, const flo
 // storage type as the unfused stem would read it back, and writes the luma
 // guide of the pixels the tile owns (its 64 x 32 interior; the scene colour
 // and the normalised input too when asked for). The network input itself
-// never reaches HBM. Phase 2: each thread computes 4 adjacent outputs x 16
+// never reaches HBM. Phase 2: each thread computes 2 adjacent outputs x 16
 // channels from the window with k_conv's accumulation order (bias, then ky,
-// kx, input channel), the weights read as shared-memory broadcasts.
+// kx, input channel), the weights read as shared-memory broadcasts. Two
+// outputs per thread keep a thread within 64 registers, so four 256-thread
+// CTAs (32 warps) share an SM and one CTA's window loads overlap another's FMAs.
 constexpr int kStemTW = 32, kStemTH = 16, kStemWinW = 2 * kStemTW + 1, kStemWinH = 2 * kStemTH + 1;
-// one float4 of padding after every 8: a quarter-warp's reads (8 threads 8
+// one float4 of padding after every 8: a quarter-warp's reads (8 threads 4
 // window columns apart) then fall into distinct banks
 constexpr int kStemRow = kStemWinW + (kStemWinW + 7) / 8;
 constexpr int kStemTaps = 9 * 4 * 4;  // [ky][kx][cin][4 float4 of output channels]
-constexpr int kStemThreads = 128, kStemWin = kStemWinH * kStemWinW;
+constexpr int kStemThreads = 256, kStemOut = 2, kStemWin = kStemWinH * kStemWinW;
 constexpr int kStemBatch = (kStemWin + 2 * kStemThreads - 1) / (2 * kStemThreads);  // two batches
 constexpr size_t kStemSmem = (size_t)(kStemWinH * kStemRow + kStemTaps) * sizeof(float4);
 __device__ __forceinline__ int stem_col(int c) { return c + (c >> 3); }
 
 // Parameter list mirrored by kStemArgCount / kStemFramesArg.
 template <typename T>
-__global__ void __launch_bounds__(kStemThreads) k_stem_fused(const float *__restrict__ frames, const StemParams p) {
+__global__ void __launch_bounds__(kStemThreads, 4) k_stem_fused(const float *__restrict__ frames, const StemParams p) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 stem_sm[];
@@ -412,23 +414,24 @@ __global__ void __launch_bounds__(kStemThreads) k_stem_fused(const float *__rest
   }
   __syncthreads();
 
-  const int ly = threadIdx.x >> 3, xg = threadIdx.x & 7;
-  const int oy = oy0 + ly, ox = ox0 + xg * 4;
+  constexpr int kGroups = kStemTW / kStemOut, kCols = 2 * kStemOut + 1;
+  const int ly = threadIdx.x / kGroups, xg = threadIdx.x % kGroups;
+  const int oy = oy0 + ly, ox = ox0 + xg * kStemOut;
   if (oy >= p.OH || ox >= p.OW) return;
-  float4 acc[4][4];
+  float4 acc[kStemOut][4];
 #pragma unroll
   for (int j = 0; j < 4; j++) {
     const float4 bj = __ldg(reinterpret_cast<const float4 *>(p.bias) + j);
 #pragma unroll
-    for (int q = 0; q < 4; q++) acc[q][j] = bj;
+    for (int q = 0; q < kStemOut; q++) acc[q][j] = bj;
   }
 #pragma unroll 1
   for (int ky = 0; ky < 3; ky++) {
     const float4 *row = win + (2 * ly + ky) * kStemRow;
-    float xs[9][4];
+    float xs[kCols][4];
 #pragma unroll
-    for (int c = 0; c < 9; c++) {
-      const float4 x = row[stem_col(8 * xg + c)];
+    for (int c = 0; c < kCols; c++) {
+      const float4 x = row[stem_col(2 * kStemOut * xg + c)];
       xs[c][0] = x.x, xs[c][1] = x.y, xs[c][2] = x.z, xs[c][3] = x.w;
     }
 #pragma unroll
@@ -440,7 +443,7 @@ __global__ void __launch_bounds__(kStemThreads) k_stem_fused(const float *__rest
         for (int j = 0; j < 4; j++) {
           const float4 wv = wr[j];
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
+          for (int q = 0; q < kStemOut; q++) {
             const float x = xs[2 * q + kx][ci];
             acc[q][j] = f4fma(make_float4(x, x, x, x), wv, acc[q][j]);
           }
@@ -450,7 +453,7 @@ __global__ void __launch_bounds__(kStemThreads) k_stem_fused(const float *__rest
   }
   T *o = static_cast<T *>(p.dst) + (((long)b * p.OH + oy) * p.OW + ox) * 16;
 #pragma unroll
-  for (int q = 0; q < 4; q++) {
+  for (int q = 0; q < kStemOut; q++) {
     if (ox + q >= p.OW) break;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
