@@ -371,6 +371,63 @@ __global__ void __launch_bounds__(kStemThreads, 4) k_stem_fused(const float *__r
   const int ix0 = 2 * ox0 - 1, iy0 = 2 * oy0 - 1, S = p.S;
   for (int i = threadIdx.x; i < kStemTaps; i += kStemThreads) wsm[i] = __ldg(reinterpret_cast<const float4 *>(p.w) + i);
   const long plane = (long)S * S;
+  // Planar frames at a 16-byte aligned address (S is a multiple of 32, so
+  // every row and every 4-column group is aligned): the window's rows are read
+  // as the 17 aligned float4 groups covering input columns ix0 - 3 .. ix0 + 64
+  // (the first group's three leading pixels unused), three channel loads per
+  // group, and the owned pixels' luma stored four at a time.
+  if (p.layout == 0 && (S & 3) == 0 && (reinterpret_cast<uintptr_t>(frames) & 15) == 0) {
+    constexpr int kGroupsX = (kStemWinW + 3 + 3) / 4, kGroupsW = kStemWinH * kGroupsX;
+    for (int g0 = 0; g0 < kGroupsW; g0 += 2 * kStemThreads) {
+      float4 c[2][3];
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int gi = g0 + u * kStemThreads + (int)threadIdx.x;
+        const int ry = gi / kGroupsX, cg = gi - ry * kGroupsX;
+        const int iy = iy0 + ry, gx = ix0 - 3 + 4 * cg;
+        c[u][0] = c[u][1] = c[u][2] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (gi < kGroupsW && iy >= 0 && iy < S && gx >= 0 && gx < S) {
+          const float4 *f = reinterpret_cast<const float4 *>(frames + b * 3 * plane + (long)iy * S + gx);
+          c[u][0] = __ldg(f), c[u][1] = __ldg(f + plane / 4), c[u][2] = __ldg(f + plane / 2);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int gi = g0 + u * kStemThreads + (int)threadIdx.x;
+        if (gi >= kGroupsW) break;
+        const int ry = gi / kGroupsX, cg = gi - ry * kGroupsX;
+        const int iy = iy0 + ry, gx = ix0 - 3 + 4 * cg;
+        const bool in_frame = iy >= 0 && iy < S && gx >= 0 && gx < S;
+        const float r4[4] = {c[u][0].x, c[u][0].y, c[u][0].z, c[u][0].w};
+        const float g4[4] = {c[u][1].x, c[u][1].y, c[u][1].z, c[u][1].w};
+        const float b4[4] = {c[u][2].x, c[u][2].y, c[u][2].z, c[u][2].w};
+        float l4[4];
+        const bool own_row = ry >= 1 && ry <= 2 * kStemTH;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int rx = 4 * cg + e - 3;
+          if (rx < 0 || rx >= kStemWinW) continue;
+          float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          l4[e] = 0.0f;
+          if (in_frame) {
+            float r = r4[e], g = g4[e], bl = b4[e];
+            const float4 o = preprocess_px(r, g, bl, p.pre);
+            v = Io<T>::round4(o);
+            l4[e] = o.w;
+            if (own_row && rx >= 1 && rx <= 2 * kStemTW && (p.scene || p.input)) {
+              const long idx = b * plane + (long)iy * S + gx + e;
+              if (p.scene) reinterpret_cast<float4 *>(p.scene)[idx] = make_float4(r, g, bl, 1.0f);
+              if (p.input) Io<T>::store4(static_cast<T *>(p.input) + idx * 4, o);
+            }
+          }
+          win[ry * kStemRow + stem_col(rx)] = v;
+        }
+        // groups 1..16 hold owned columns only (rx 1..64); group 0 owns none
+        if (in_frame && own_row && cg >= 1 && cg <= 2 * kStemTW / 4)
+          *reinterpret_cast<float4 *>(p.luma + b * plane + (long)iy * S + gx) = make_float4(l4[0], l4[1], l4[2], l4[3]);
+      }
+    }
+  } else
   // the window's pixels in batches of kStemBatch per thread, all loads of a
   // batch in flight before any is used
   for (int i0 = 0; i0 < kStemWin; i0 += kStemBatch * kStemThreads) {

@@ -47,3 +47,24 @@ def test_chunked_host_forward_matches_device_chunks(torch, n, chunks):
     torch.cuda.synchronize()
     assert float(np.abs(whole.cpu().numpy() - got).max()) <= 1e-5
     model.destroy()
+
+
+def test_frames_at_any_4_byte_offset_match_aligned(torch):
+    """The fused preprocess+stem reads planar frames as float4 groups when the
+    pointer is 16-byte aligned and pixel by pixel otherwise; both give the same bits."""
+    import illumina
+    from illumina import _lib
+    S, n = 64, 3
+    model = illumina.createDepthModel(illumina.buildArchitecture(S), synthSeed=5, maxBatch=n, device=0)
+    frames = torch.empty((n, 3, S, S), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().illumina_generate_frames(0, 7, n, S, frames.data_ptr(), None))
+    want = model.forward(frames).cpu().numpy()
+    for off in (1, 2, 3):
+        buf = torch.zeros(n * 3 * S * S + 4, dtype=torch.float32, device="cuda")
+        view = buf[off:off + n * 3 * S * S].view(n, 3, S, S)
+        view.copy_(frames)
+        assert view.data_ptr() % 16 != 0
+        got = model.forward(view)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(got.cpu().numpy(), want)
+    model.destroy()
