@@ -1,4 +1,4 @@
-"""The host-buffer forward runs in frame chunks (16, 48, 64 ..., 48, 16 frames from 128 on), uploads and
+"""The host-buffer forward runs in frame chunks (16, 32, 48, ..., then 16 frames, from 128 on), uploads and
 downloads on their own streams overlapping the neighbouring chunks' graphs.
 Frames are independent, so the result must equal, bit for bit, device-pointer
 forwards over the same chunk sizes (the launch plan depends on the batch size,
@@ -19,7 +19,7 @@ def torch():
     return torch
 
 
-@pytest.mark.parametrize("n,chunks", [(40, [20, 20]), (33, [17, 16]), (130, [16, 48, 50, 16]), (256, [16, 48, 64, 64, 48, 16])])
+@pytest.mark.parametrize("n,chunks", [(40, [20, 20]), (33, [17, 16]), (130, [16, 32, 48, 18, 16]), (256, [16, 32, 48, 64, 80, 16])])
 def test_chunked_host_forward_matches_device_chunks(torch, n, chunks):
     import illumina
     from illumina import _lib
