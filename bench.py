@@ -398,6 +398,32 @@ def scene_and_metrics(model, stream, ev0, ev1, batch=64, reps=5):
             "batch": batch, "outputs": "rgb 3x448x448 f32 + truth 448x448x2 f32 per frame"}
 
 
+def source_sampling(model, stream, ev0, ev1, batch=64, reps=10):
+    """8-bit camera frames (1920x1080 RGBA) sampled to the 448 network input with
+    the blit's centre crop (cropTransform) folded into makePreprocess's uv
+    transform: `batch` frames per launch, device buffers."""
+    import torch
+    import illumina
+
+    w, h = 1920, 1080
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    src = torch.randint(0, 256, (batch, h, w, 4), dtype=torch.uint8, device="cuda", generator=g)
+    frames = torch.empty((batch, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    t = illumina.cropTransform(w, h)
+    for _ in range(3):
+        model.sampleSource(src, t[:2], t[2:], frames=frames, stream=stream)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(reps):
+        model.sampleSource(src, t[:2], t[2:], frames=frames, stream=stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / reps
+    return {"us_per_frame": 1000.0 * ms / batch, "ms_per_launch": ms, "batch": batch,
+            "source": f"{w}x{h} RGBA8, centre crop, bilinear clamp-to-edge", "output": "3x448x448 f32 planar"}
+
+
 def bf16_throughput(local_rank, stream, ev0, ev1, batch=256, reps=5):
     """BF16 weights and activations (fp32 accumulation on tcgen05) at batch 256 on uniform
     frames: frames/s on device-resident inputs."""
@@ -542,6 +568,7 @@ def run_ours(args, rank, local_rank, world):
         extras["batch1_us_per_frame"] = 1000.0 * ev0.elapsed_time(ev1) / reps
         extras["depth_relight_1080p"] = depth_relight_frame(model, b1_frames, ring, stream, ev0, ev1)
         extras["scene_448"] = scene_and_metrics(model, stream, ev0, ev1)
+        extras["source_1080p"] = source_sampling(model, stream, ev0, ev1)
         del b1_frames
     if rank == 0 and not args.no_extras and args.precision == "f32":
         extras["bf16_b256"] = bf16_throughput(local_rank, stream, ev0, ev1)
