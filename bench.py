@@ -366,6 +366,7 @@ def scene_and_metrics(model, stream, ev0, ev1, batch=64, reps=5):
     from illumina import _lib, renderScenes, sceneParams
 
     lib = _lib.lib()
+    batch = min(batch, model.maxBatch)  # the scene frames also go through the model once
     params = [sceneParams(0.25 * i, True) for i in range(batch)]
     rgb = torch.empty((batch, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
     truth = torch.empty((batch, SIZE, SIZE, 2), dtype=torch.float32, device="cuda")
