@@ -79,12 +79,15 @@ struct GemmOp {
   const float *head_w = nullptr;
   float head_b = 0.0f;
   float *head_dst = nullptr;
+  // Tensor engine: cycles a pipeline wait may take before the kernel gives up
+  // and sets *err (0 = the default, ~1 s).
+  long long wait_cycles = 0;
 };
 
 cudaError_t gemm(int T, const GemmOp &op, cudaStream_t st);
 
-// Tensor-core (tcgen05) engine for the same ops (tc_gemm.cu). The weights of
-// each op are pre-packed into swizzled per-(n tile, K slab) shared-memory
+// Tensor-core (tcgen05) engine for the same ops. The weights of each op are
+// pre-packed (tc_pack.cu) into swizzled per-(n tile, K slab) shared-memory
 // images: tf32 hi/lo pairs for fp32 storage, bf16 for bf16 storage.
 struct TcWeights {
   int N = 0, K = 0;
@@ -96,11 +99,9 @@ struct TcWeights {
 };
 TcWeights tc_plan(int T, int N, int K);
 cudaError_t tc_pack(int T, const float *w, int N, int K, const TcWeights &plan, uint8_t *out, cudaStream_t st);
-size_t tc_smem_bytes(int T, const TcWeights &plan);
-cudaError_t tc_gemm(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st);
 // Persistent warp-specialised variant for pointwise (mode 0) and lateral
 // (mode 2): TMA A tiles, bulk-copied weight images, double-buffered TMEM
-// accumulators (tc_pw.cu). Same weight images as tc_gemm.
+// accumulators (tc_pw.cu).
 cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t *wimg, int *err, cudaStream_t st);
 
 // Depthwise->pointwise (mode 1) on the persistent kernel of tc_dw.cu: the

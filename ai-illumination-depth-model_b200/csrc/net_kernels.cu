@@ -1061,45 +1061,166 @@ __global__ void k_gen_uniform(uint32_t seed0, int n, int S, float *out) {
   out[i] = (float)mb32_at(seed0 + (uint32_t)f, j);
 }
 
-// Blob frames: per channel 8 blobs (cx, cy in [0,S), sx, sy in [20,120],
-// theta in [0,pi), amplitude in [0,1]) = 144 draws, then per value a
-// Box-Muller N(0, 0.02) noise sample (2 draws) in (c, y, x) order.
-__global__ void k_gen_blobs(uint32_t seed0, int n, int S, float *out) {
-  long per = 3L * S * S;
-  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= per * n) return;
-  int f = (int)(i / per);
-  long j = i - (long)f * per;
-  int c = (int)(j / ((long)S * S));
-  long pix = j - (long)c * S * S;
-  int y = (int)(pix / S), x = (int)(pix % S);
-  uint32_t seed = seed0 + (uint32_t)f;
-  float v = 0.0f;
-  for (int bidx = 0; bidx < 8; bidx++) {
-    uint32_t d = (uint32_t)((c * 8 + bidx) * 6);
-    float cxp = (float)(mb32_at(seed, d) * S), cyp = (float)(mb32_at(seed, d + 1) * S);
-    float sx = (float)(20.0 + 100.0 * mb32_at(seed, d + 2)), sy = (float)(20.0 + 100.0 * mb32_at(seed, d + 3));
-    float th = (float)(M_PI * mb32_at(seed, d + 4));
-    float amp = (float)mb32_at(seed, d + 5);
-    float dx = x + 0.5f - cxp, dy = y + 0.5f - cyp;
-    float cs = cosf(th), sn = sinf(th);
-    float u = cs * dx + sn * dy, w = -sn * dx + cs * dy;
-    v += amp * expf(-0.5f * (u * u / (sx * sx) + w * w / (sy * sy)));
+// Blob frames (smooth procedural images): per frame seed and channel c,
+// 8 anisotropic Gaussian blobs from draws (c*8 + b)*6 .. +5 of the frame's
+// mulberry32 stream -- centre (u0*S, u1*S), sigma_x = 20 + 100*u2,
+// sigma_y = 20 + 100*u3 pixels, rotation u4*pi, amplitude u5 -- summed at
+// the pixel centre, plus N(0, 0.02) Box-Muller noise on draws 144 + 2j and
+// 145 + 2j (j = the value's (c, y, x) index, u clamped to 1e-9), clamped to
+// [0, 1]. Every step is an IEEE double add, multiply, divide, square root or
+// fused multiply-add with round-to-nearest in a fixed order (the intrinsics
+// below are never contracted or reassociated), and exp / log / sin / cos are
+// written out from their series: exp by Cody-Waite reduction with ln 2 split
+// in two and the Taylor series to r^13/13!; log by the atanh series
+// log m = 2 atanh((m-1)/(m+1)) on m in [sqrt(1/2), sqrt(2)]; sin and cos by
+// their Taylor series on [-pi/2, pi/2]. A host evaluation of the same
+// operations therefore gives the same bits, and the functions are within a
+// few ulp of the exact ones.
+namespace detm {
+
+__device__ __constant__ double kExpC[12] = {0.5, 0.16666666666666666, 0.041666666666666664, 0.008333333333333333,
+                                            0.001388888888888889, 0.0001984126984126984, 2.48015873015873e-05,
+                                            2.7557319223985893e-06, 2.755731922398589e-07, 2.505210838544172e-08,
+                                            2.08767569878681e-09, 1.6059043836821613e-10};
+__device__ __constant__ double kLogC[12] = {0.3333333333333333, 0.2, 0.14285714285714285, 0.1111111111111111,
+                                            0.09090909090909091, 0.07692307692307693, 0.06666666666666667,
+                                            0.058823529411764705, 0.05263157894736842, 0.047619047619047616,
+                                            0.043478260869565216, 0.04};
+__device__ __constant__ double kCosC[12] = {-0.5, 0.041666666666666664, -0.001388888888888889, 2.48015873015873e-05,
+                                            -2.755731922398589e-07, 2.08767569878681e-09, -1.1470745597729725e-11,
+                                            4.779477332387385e-14, -1.5619206968586225e-16, 4.110317623312165e-19,
+                                            -8.896791392450574e-22, 1.6117375710961184e-24};
+__device__ __constant__ double kSinC[11] = {-0.16666666666666666, 0.008333333333333333, -0.0001984126984126984,
+                                            2.7557319223985893e-06, -2.505210838544172e-08, 1.6059043836821613e-10,
+                                            -7.647163731819816e-13, 2.8114572543455206e-15, -8.22063524662433e-18,
+                                            1.9572941063391263e-20, -3.868170170630684e-23};
+constexpr double kLn2Hi = 0.6931471803691238;  // 0x1.62e42feep-1: k * hi is exact
+constexpr double kLn2Lo = 1.9082149292705877e-10;
+constexpr double kInvLn2 = 1.4426950408889634;
+constexpr double kPi = 3.141592653589793;
+constexpr double kPiHalf = 1.5707963267948966;
+constexpr double kTwoPi = 6.283185307179586;
+constexpr double kSqrt2 = 1.4142135623730951;
+
+// exp(x) for x <= 0 (0 below -708)
+__device__ double exp_neg(double x) {
+  if (x < -708.0) return 0.0;
+  const double kd = floor(__fma_rn(x, kInvLn2, 0.5));
+  double r = __fma_rn(-kd, kLn2Hi, x);
+  r = __fma_rn(-kd, kLn2Lo, r);
+  double p = kExpC[11];
+#pragma unroll
+  for (int i = 10; i >= 0; i--) p = __fma_rn(p, r, kExpC[i]);
+  p = __fma_rn(p, r, 1.0);
+  p = __fma_rn(p, r, 1.0);
+  return __dmul_rn(p, __longlong_as_double((long long)((int)kd + 1023) << 52));
+}
+
+// log(u) for normal u > 0
+__device__ double log_pos(double u) {
+  unsigned long long b = (unsigned long long)__double_as_longlong(u);
+  int e = (int)((b >> 52) & 0x7ff) - 1023;
+  double m = __longlong_as_double((long long)((b & 0x000fffffffffffffull) | 0x3ff0000000000000ull));
+  if (m > kSqrt2) {
+    m = __dmul_rn(m, 0.5);
+    e += 1;
   }
-  uint32_t nd = 144u + 2u * (uint32_t)j;
+  const double s = __ddiv_rn(__dsub_rn(m, 1.0), __dadd_rn(m, 1.0));
+  const double z = __dmul_rn(s, s);
+  double p = kLogC[11];
+#pragma unroll
+  for (int i = 10; i >= 0; i--) p = __fma_rn(p, z, kLogC[i]);
+  p = __fma_rn(p, z, 1.0);
+  const double lm = __dmul_rn(__dadd_rn(s, s), p);
+  const double ed = (double)e;
+  return __fma_rn(ed, kLn2Hi, __fma_rn(ed, kLn2Lo, lm));
+}
+
+__device__ double cos_poly(double t) {  // |t| <= pi/2
+  const double z = __dmul_rn(t, t);
+  double p = kCosC[11];
+#pragma unroll
+  for (int i = 10; i >= 0; i--) p = __fma_rn(p, z, kCosC[i]);
+  return __fma_rn(p, z, 1.0);
+}
+
+__device__ double sin_poly(double t) {  // |t| <= pi/2
+  const double z = __dmul_rn(t, t);
+  double p = kSinC[10];
+#pragma unroll
+  for (int i = 9; i >= 0; i--) p = __fma_rn(p, z, kSinC[i]);
+  p = __fma_rn(p, z, 1.0);
+  return __dmul_rn(t, p);
+}
+
+// cos(2 pi v), v in [0, 1) a multiple of 2^-32 (the reductions are exact)
+__device__ double cos2pi(double v) {
+  const double a = fabs(__dsub_rn(v, floor(__dadd_rn(v, 0.5))));
+  if (a <= 0.25) return cos_poly(__dmul_rn(a, kTwoPi));
+  return -cos_poly(__dmul_rn(__dsub_rn(0.5, a), kTwoPi));
+}
+
+}  // namespace detm
+
+struct BlobParams {
+  double cx, cy, hx, hy, cs, sn, amp;
+};
+
+// grid (ceil(S*S / 256), 3 channels, n frames); 256 threads, one value each
+__global__ void __launch_bounds__(256) k_gen_blobs(uint32_t seed0, int S, float *out) {
+  __shared__ BlobParams bl[8];
+  const int c = blockIdx.y, f = blockIdx.z;
+  const uint32_t seed = seed0 + (uint32_t)f;
+  if (threadIdx.x < 8) {
+    const int b = threadIdx.x;
+    const uint32_t d = (uint32_t)((c * 8 + b) * 6);
+    BlobParams o;
+    o.cx = __dmul_rn(mb32_at(seed, d), (double)S);
+    o.cy = __dmul_rn(mb32_at(seed, d + 1), (double)S);
+    const double sx = __fma_rn(mb32_at(seed, d + 2), 100.0, 20.0);
+    const double sy = __fma_rn(mb32_at(seed, d + 3), 100.0, 20.0);
+    o.hx = __ddiv_rn(0.5, __dmul_rn(sx, sx));
+    o.hy = __ddiv_rn(0.5, __dmul_rn(sy, sy));
+    const double t = __dsub_rn(__dmul_rn(mb32_at(seed, d + 4), detm::kPi), detm::kPiHalf);  // theta - pi/2
+    o.cs = -detm::sin_poly(t);
+    o.sn = detm::cos_poly(t);
+    o.amp = mb32_at(seed, d + 5);
+    bl[b] = o;
+  }
+  __syncthreads();
+  const long plane = (long)S * S;
+  const long pix = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= plane) return;
+  const int y = (int)(pix / S), x = (int)(pix - (long)y * S);
+  const double px = (double)x + 0.5, py = (double)y + 0.5;
+  double v = 0.0;
+#pragma unroll 1
+  for (int b = 0; b < 8; b++) {
+    const BlobParams B = bl[b];
+    const double dx = __dsub_rn(px, B.cx), dy = __dsub_rn(py, B.cy);
+    const double u = __fma_rn(B.cs, dx, __dmul_rn(B.sn, dy));
+    const double w = __fma_rn(B.cs, dy, -__dmul_rn(B.sn, dx));
+    const double q = __fma_rn(__dmul_rn(u, u), B.hx, __dmul_rn(__dmul_rn(w, w), B.hy));
+    v = __fma_rn(B.amp, detm::exp_neg(-q), v);
+  }
+  const long j = (long)c * plane + pix;
+  const uint32_t nd = 144u + 2u * (uint32_t)j;
   double uu = mb32_at(seed, nd);
   if (uu < 1e-9) uu = 1e-9;
-  double vv = mb32_at(seed, nd + 1);
-  float g = (float)(sqrt(-2.0 * log(uu)) * cos(2.0 * M_PI * vv));
-  v += 0.02f * g;
-  out[i] = fminf(fmaxf(v, 0.0f), 1.0f);
+  const double g = __dmul_rn(__dsqrt_rn(__dmul_rn(-2.0, detm::log_pos(uu))), detm::cos2pi(mb32_at(seed, nd + 1)));
+  v = __fma_rn(0.02, g, v);
+  v = v < 0.0 ? 0.0 : (v > 1.0 ? 1.0 : v);
+  out[(long)f * 3 * plane + j] = __double2float_rn(v);
 }
 
 cudaError_t generate_frames(int kind, uint32_t seed0, int n, int S, float *out, cudaStream_t st) {
   long total = 3L * S * S * n;
   if (total == 0) return cudaSuccess;
   if (kind == 0) k_gen_uniform<<<blocks_for(total, 256), 256, 0, st>>>(seed0, n, S, out);
-  else k_gen_blobs<<<blocks_for(total, 256), 256, 0, st>>>(seed0, n, S, out);
+  else {
+    if (n > 65535) return cudaErrorInvalidValue;
+    k_gen_blobs<<<dim3(blocks_for((long)S * S, 256), 3, (unsigned)n), 256, 0, st>>>(seed0, S, out);
+  }
   return cudaGetLastError();
 }
 

@@ -5,7 +5,9 @@
 // kernel's [k*k][C] layout in a temporary buffer from cudaMallocAsync. This
 // variant repacks into a fixed, file-scope device array instead, so the call
 // performs no allocation of any kind: it only launches the repack kernel and
-// the fused dw->pw kernel.
+// the fused dw->pw kernel. It always runs the SIMT engine's kernel (k_gemm),
+// whatever illumina_set_op_engine selected: the tensor engine would need its
+// weight images in an allocation.
 //
 // The array belongs to every GPU that loads this library and stays reserved
 // until the process exits. Every call on a device shares it and it keeps the
@@ -36,7 +38,7 @@ std::vector<float *> g_addr;  // per device ordinal: device address of g_dw_pack
 
 // Host code must not use g_dw_packed's name as a device address: resolve it
 // once per device, with that device current.
-float *packed_scratch_for_current_device() {
+float *packed_scratch_for_current_device(cudaStream_t st) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess)
@@ -44,6 +46,14 @@ float *packed_scratch_for_current_device() {
   std::lock_guard<std::mutex> lock(g_mu);
   if ((size_t)dev >= g_addr.size()) g_addr.resize(dev + 1, nullptr);
   if (!g_addr[dev]) {
+    // resolving the address is not a stream operation and may not be legal
+    // while a capture is open: the first call on a device must come first
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(st, &cs);
+    if (e != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+      throw illumina::Error(ILLUMINA_INVALID_ARG,
+                            "dwpw_noalloc: the first call on a device must precede stream capture (the stream is "
+                            "being captured)");
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_dw_packed);
     if (e != cudaSuccess || !p)
@@ -76,7 +86,7 @@ extern "C" illumina_status illumina_op_dwpw_noalloc(const float *src, int in_h, 
             "dwpw_noalloc: in_c*k*k = " + std::to_string((size_t)in_c * k * k) + " exceeds the fixed scratch of " +
                 std::to_string(kMaxPackedFloats) + " floats; use illumina_op_dwpw");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    float *packed = packed_scratch_for_current_device();
+    float *packed = packed_scratch_for_current_device(st);
     cudaError_t e = illumina::gpu::pack_dw(dw_w, in_c, k, packed, 0, st);
     if (e != cudaSuccess) throw illumina::Error(ILLUMINA_CUDA_ERROR, std::string("dwpw_noalloc pack: ") + cudaGetErrorString(e));
     int pad = (k - 1) >> 1;

@@ -145,7 +145,12 @@ struct illumina_model {
   std::vector<gpu::TcWeights> tcw;   // per op (pw / dwpw / lateral)
   std::vector<size_t> tc_off;        // per op: byte offset into d_wimg
   uint8_t *d_wimg = nullptr;         // tensor-core weight images
-  int *d_err = nullptr;              // set by a kernel that gave up a bounded wait
+  // Error word, set (plain store) by a kernel that gave up a bounded wait:
+  // pinned host memory mapped into the device, so the host reads it after a
+  // launch without a copy on the stream.
+  volatile int *h_err = nullptr;
+  int *d_err = nullptr;              // device address of h_err
+  long long wait_cycles = 0;         // tensor kernels' pipeline wait limit (0: the kernels' default)
   float *d_splitk = nullptr;         // split-K partial tiles of the tensor dw->pw kernel
   int *d_splitk_cnt = nullptr;       // its per-item arrival counters (zero between launches)
   int stem_fused_op = -1;            // conv op folded into the preprocess launch, or -1
@@ -181,7 +186,7 @@ illumina_model::~illumina_model() {
   cudaFree(d_stage_out);
   cudaFree(d_stage_low);
   cudaFree(d_wimg);
-  cudaFree(d_err);
+  if (h_err) cudaFreeHost((void *)h_err);
   cudaFree(d_splitk);
   cudaFree(d_splitk_cnt);
   if (ev_join) cudaEventDestroy(ev_join);
@@ -342,6 +347,7 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
         const TensorShape &so = a.shape(op.out);
         gpu::GemmOp g;
         g.n = n;
+        g.wait_cycles = m.wait_cycles;
         g.dst = m.tensor(op.out);
         g.bias = w.b;
         g.w = w.w;
@@ -505,6 +511,23 @@ int host_chunks(int n, int *sizes) {
   return k;
 }
 
+// Reports a bounded device wait that gave up (the kernels set the model's
+// error word and left the rest of their work undone, so the outputs of the
+// forward that ran them are undefined): clears the word, returns the split-K
+// arrival counters (which a unit that gave up may have left non-zero) to zero
+// and throws TIMEOUT. `when` says which call's kernels the word covers.
+void check_timeout(illumina_model &m, const char *when) {
+  if (!m.h_err || *m.h_err == 0) return;
+  cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+  *m.h_err = 0;
+  if (m.d_splitk_cnt) {
+    cuda_check(cudaMemsetAsync(m.d_splitk_cnt, 0, kSplitKItems * sizeof(int), m.stream), "clear split-K counters");
+    cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+  }
+  throw Error(ILLUMINA_TIMEOUT, std::string("a tensor-core kernel gave up a bounded wait (") + when +
+                                    "); the outputs of that forward are undefined, the model is usable again");
+}
+
 void run_forward(illumina_model &m, const float *frames, int n, int layout, float *disp, float *low,
                  cudaStream_t caller, int mode) {
   if (n < 1 || n > m.opts.max_batch)
@@ -514,6 +537,8 @@ void run_forward(illumina_model &m, const float *frames, int n, int layout, floa
     throw Error(ILLUMINA_INVALID_ARG, "forward: unknown frame layout " + std::to_string(layout));
   if (!frames) throw Error(ILLUMINA_INVALID_ARG, "forward: frames is null");
   cuda_check(cudaSetDevice(m.device), "cudaSetDevice");
+  // a forward queued by an earlier call on device buffers may have given up
+  check_timeout(m, "in an earlier call on this model");
   const int S = m.arch.input_size;
   const long frame_floats = (layout == ILLUMINA_FRAME_RGB_PLANAR ? 3L : 4L) * S * S;
   const long disp_floats = (long)S * S, low_floats = (long)(S / 2) * (S / 2);
@@ -569,6 +594,7 @@ void run_forward(illumina_model &m, const float *frames, int n, int layout, floa
     cuda_check(cudaEventRecord(m.ev_done, m.stream), "event record");
     cuda_check(cudaStreamWaitEvent(caller, m.ev_done, 0), "caller wait");
     cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+    check_timeout(m, "in this call");
     return;
   }
 
@@ -601,7 +627,10 @@ void run_forward(illumina_model &m, const float *frames, int n, int layout, floa
                "depth_low D2H");
   cuda_check(cudaEventRecord(m.ev_done, m.stream), "event record");
   cuda_check(cudaStreamWaitEvent(caller, m.ev_done, 0), "caller wait");
-  if (sync) cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+  if (sync) {
+    cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+    check_timeout(m, "in this call");
+  }
 }
 
 void build_model(illumina_model &m, const illumina_model_options &o) {
@@ -725,8 +754,15 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
     throw Error(ILLUMINA_INVALID_ARG, "createDepthModel: unknown gemm engine " + std::to_string(o.gemm_engine));
   m.engine = o.gemm_engine;
   plan_head_fusion(m);
-  cuda_check(cudaMalloc(&m.d_err, sizeof(int)), "cudaMalloc error flag");
-  cuda_check(cudaMemsetAsync(m.d_err, 0, sizeof(int), m.stream), "clear error flag");
+  {
+    void *h = nullptr;
+    cuda_check(cudaHostAlloc(&h, sizeof(int), cudaHostAllocMapped), "cudaHostAlloc error word");
+    m.h_err = (volatile int *)h;
+    *m.h_err = 0;
+    void *d = nullptr;
+    cuda_check(cudaHostGetDevicePointer(&d, h, 0), "error word device address");
+    m.d_err = (int *)d;
+  }
   if (o.gemm_engine == ILLUMINA_ENGINE_TENSOR) {
     cuda_check(cudaMalloc(&m.d_splitk, kSplitKBytes), "cudaMalloc split-K workspace");
     cuda_check(cudaMalloc(&m.d_splitk_cnt, kSplitKItems * sizeof(int)), "cudaMalloc split-K counters");
@@ -983,6 +1019,27 @@ illumina_status illumina_model_record(illumina_model *m, const float *frame, int
   ILL_CATCH
 }
 
+illumina_status illumina_model_sync(illumina_model *m) {
+  ILL_TRY
+  require(m, "sync: null model");
+  cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+  cuda_check(cudaStreamSynchronize(m->stream), "synchronize");
+  check_timeout(*m, "in a forward queued since the last check");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_model_set_wait_limit(illumina_model *m, long long cycles) {
+  ILL_TRY
+  require(m && cycles >= 0, "setWaitLimit: bad arguments");
+  cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+  cuda_check(cudaStreamSynchronize(m->stream), "synchronize");
+  m->wait_cycles = cycles;
+  m->clear_graphs();  // the limit is a kernel parameter of the captured launches
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
 illumina_status illumina_model_swap_history(illumina_model *m) {
   ILL_TRY
   require(m, "swapHistory: null model");
@@ -1002,8 +1059,8 @@ illumina_status illumina_model_depth_slot(illumina_model *m, int index, const fl
   ILL_CATCH
 }
 
-illumina_status illumina_model_debug_tensor(illumina_model *m, const char *name, float *out, size_t cap, int *h,
-                                            int *w, int *c, int *live_at_end) {
+illumina_status illumina_model_debug_tensor_frame(illumina_model *m, const char *name, int frame, float *out,
+                                                  size_t cap, int *h, int *w, int *c, int *live_at_end) {
   ILL_TRY
   require(m && name, "debugTensor: null argument");
   std::string n(name);
@@ -1011,6 +1068,8 @@ illumina_status illumina_model_debug_tensor(illumina_model *m, const char *name,
   auto as = m->plan.assignment.find(n);
   if (ts == m->arch.tensors.end() || as == m->plan.assignment.end())
     throw Error(ILLUMINA_INVALID_ARG, "debugTensor: unknown tensor " + n);
+  require(frame >= 0 && frame < m->opts.max_batch,
+          "debugTensor: frame " + std::to_string(frame) + " outside [0, " + std::to_string(m->opts.max_batch) + ")");
   const TensorShape &s = ts->second;
   if (h) *h = s.h;
   if (w) *w = s.w;
@@ -1024,14 +1083,25 @@ illumina_status illumina_model_debug_tensor(illumina_model *m, const char *name,
   float *tmp = nullptr;
   cuda_check(cudaMalloc(&tmp, sizeof(float) * count), "cudaMalloc");
   cudaError_t e;
-  if (n == "depth_low") e = gpu::expand4((const float *)m->tensor(n), (long)s.h * s.w, tmp, m->stream);
-  else e = gpu::to_f32(m->T, m->tensor(n), count, tmp, m->stream);
+  // frames are stored one after another: depth_low as one fp32 channel per
+  // pixel, every other tensor as h x w x c elements of the model's type
+  const char *base = (const char *)m->tensor(n);
+  if (n == "depth_low")
+    e = gpu::expand4((const float *)(base + (size_t)frame * s.h * s.w * sizeof(float)), (long)s.h * s.w, tmp,
+                     m->stream);
+  else
+    e = gpu::to_f32(m->T, base + (size_t)frame * count * m->elt, count, tmp, m->stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(out, tmp, sizeof(float) * count, cudaMemcpyDefault, m->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
   cudaFree(tmp);
   cuda_check(e, "debugTensor copy");
   return ILLUMINA_OK;
   ILL_CATCH
+}
+
+illumina_status illumina_model_debug_tensor(illumina_model *m, const char *name, float *out, size_t cap, int *h,
+                                            int *w, int *c, int *live_at_end) {
+  return illumina_model_debug_tensor_frame(m, name, 0, out, cap, h, w, c, live_at_end);
 }
 
 illumina_status illumina_model_stats(const illumina_model *m, illumina_stats *out) {
@@ -1047,10 +1117,9 @@ illumina_status illumina_model_stats(const illumina_model *m, illumina_stats *ou
   out->precision = m->opts.precision;
   out->input_size = m->arch.input_size;
   out->gemm_engine = m->engine;
-  int flag = 0;
   cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
-  cuda_check(cudaMemcpy(&flag, m->d_err, sizeof(int), cudaMemcpyDeviceToHost), "read error flag");
-  out->device_error = flag;
+  cuda_check(cudaStreamSynchronize(m->stream), "synchronize");
+  out->device_error = m->h_err ? *m->h_err : 0;
   return ILLUMINA_OK;
   ILL_CATCH
 }

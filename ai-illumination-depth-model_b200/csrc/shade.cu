@@ -349,16 +349,18 @@ cudaError_t shade(const float *depth, int dw, int dh, int dch, const float *albe
 __global__ void k_resize(const float *src, int sw, int sh, float *dst, int dw, int dh) {
   int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
   if (x >= dw || y >= dh) return;
-  float u = ((float)x + 0.5f) / (float)dw, v = ((float)y + 0.5f) / (float)dh;
-  float tx = u * (float)sw - 0.5f, ty = v * (float)sh - 0.5f;
+  // every operation rounded on its own (no contraction), so the result is
+  // the same float as a host evaluation in this order
+  float u = __fdiv_rn((float)x + 0.5f, (float)dw), v = __fdiv_rn((float)y + 0.5f, (float)dh);
+  float tx = __fsub_rn(__fmul_rn(u, (float)sw), 0.5f), ty = __fsub_rn(__fmul_rn(v, (float)sh), 0.5f);
   float fx0 = floorf(tx), fy0 = floorf(ty);
-  float fx = tx - fx0, fy = ty - fy0;
+  float fx = __fsub_rn(tx, fx0), fy = __fsub_rn(ty, fy0);
   int x0 = min(max((int)fx0, 0), sw - 1), x1 = min(max((int)fx0 + 1, 0), sw - 1);
   int y0 = min(max((int)fy0, 0), sh - 1), y1 = min(max((int)fy0 + 1, 0), sh - 1);
   float a = __ldg(src + (long)y0 * sw + x0), b = __ldg(src + (long)y0 * sw + x1);
   float c = __ldg(src + (long)y1 * sw + x0), d = __ldg(src + (long)y1 * sw + x1);
-  float top = a + (b - a) * fx, bot = c + (d - c) * fx;
-  dst[(long)y * dw + x] = top + (bot - top) * fy;
+  float top = __fadd_rn(a, __fmul_rn(__fsub_rn(b, a), fx)), bot = __fadd_rn(c, __fmul_rn(__fsub_rn(d, c), fx));
+  dst[(long)y * dw + x] = __fadd_rn(top, __fmul_rn(__fsub_rn(bot, top), fy));
 }
 
 cudaError_t resize_bilinear(const float *src, int sw, int sh, float *dst, int dw, int dh, cudaStream_t st) {

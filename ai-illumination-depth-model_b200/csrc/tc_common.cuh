@@ -17,7 +17,7 @@ namespace tcx {
 
 constexpr int kTileM = 128;
 constexpr uint32_t kAImage = kTileM * 128;  // one 128-row x 128-byte operand image
-constexpr long long kWaitCycles = 1ll << 31;
+constexpr long long kWaitCycles = 1ll << 31;  // default wait limit: ~1.1 s at 1.965 GHz
 // A waiting thread stays suspended in try_wait until the phase completes or
 // this many nanoseconds pass, instead of re-polling at the hardware's default
 // interval (polling warps take issue slots from the working ones).
@@ -33,21 +33,35 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity, uint32_t suspend_ns = kSuspendNs) {
   uint32_t ok;
   asm volatile(
       "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of parity `parity`; false once ~2^31 cycles pass.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait for the phase of parity `parity`; false once `limit` cycles
+// pass. The pipeline waits of a launch take the launch's limit (a kernel
+// parameter, kWaitCycles unless the caller lowers it); the waits with which a
+// role that gave up drains its own copies and MMAs before the CTA leaves keep
+// kWaitCycles, so nothing is in flight when TMEM is released.
+// A limit below the suspend interval also shortens each suspension (to about
+// the limit at 2 cycles per ns), so a tiny limit gives up at the first probe
+// that finds the phase incomplete.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit = kWaitCycles) {
+  const uint32_t hint = limit >= 2ll * kSuspendNs ? kSuspendNs : (uint32_t)(limit / 2 + 1);
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity))
-    if (clock64() - t0 > kWaitCycles) return false;
+  while (!mbar_try_wait(bar, parity, hint))
+    if (clock64() - t0 > limit) return false;
   return true;
+}
+// Records that a role gave up a wait: a plain store to the error word (host
+// memory mapped into the device's address space, read by the host after the
+// launch; nothing else writes it from the device).
+__device__ __forceinline__ void report_gave_up(int *err) {
+  if (err) *reinterpret_cast<volatile int *>(err) = 1;
 }
 // Per-warpgroup register budget changes (every warp of the warpgroup runs
 // them): the block is launched with a uniform count and the roles trade

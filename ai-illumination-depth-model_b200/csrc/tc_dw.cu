@@ -270,6 +270,7 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   const int terms = T == F32 ? 2 : 1;
   tcd::Params p;
   p.wimg = wimg, p.dwblk = wimg + plan.dw_off, p.err = err;
+  p.wait = op.wait_cycles > 0 ? op.wait_cycles : tcx::kWaitCycles;
   p.epi.bias = op.bias, p.epi.res = op.res, p.epi.coarse = nullptr, p.epi.dst = op.dst;
   p.epi.N = op.N, p.epi.act = op.act, p.epi.OH = op.OH, p.epi.OW = op.OW, p.epi.n_tile = plan.n_tile;
   p.tiles_x = (op.OW + tl.tw - 1) / tl.tw;

@@ -77,6 +77,7 @@ struct Params {
   const uint8_t *dwblk;  // [slab][KS*KS + 1][slab_c] f32: taps, then bias
   EpiArgs epi;           // OH, OW: output spatial size
   int *err;
+  long long wait;  // cycles a pipeline wait may take before the role gives up
   float *ws;  // split-K partial tiles [item][split][128][n_tile] (ksplit > 1)
   int *cnt;   // split-K arrival counters [item], zero between launches
   int tiles_x, tiles_y, n_tiles, slabs, items, ksplit, spk, total;  // total = items * ksplit units
@@ -265,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  const long long lim = p.wait;
 
   if (warp < kXfWarp0) {
     reg_dealloc<kProducerRegs>();
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
           const Item it = decode<SPLIT>(p, t);
           for (int s = it.s0; s < it.s1; s++) {
-            if (!mbar_wait(&h_empty[hs], hph ^ 1u)) {
+            if (!mbar_wait(&h_empty[hs], hph ^ 1u, lim)) {
               ok = false;
               break;
             }
@@ -310,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
             const Item it = decode<SPLIT>(p, t);
             const int nt = it.nt;
             for (int s = it.s0; s < it.s1; s++) {
-              if (!mbar_wait(&g_empty[gs], gph ^ 1u)) {
+              if (!mbar_wait(&g_empty[gs], gph ^ 1u, lim)) {
                 ok = false;
                 break;
               }
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     } else if (warp == kMmaWarp) {
       // ------------------------------------------------------- MMA issuer
       if (lane == 0) {
-        if (p.b_res && !mbar_wait(b_full, 0)) ok = false;
+        if (p.b_res && !mbar_wait(b_full, 0, lim)) ok = false;
         int gs = 0, acc = 0;
         uint32_t gph = 0, acc_phase = 0;
         const uint32_t idesc = instr_desc(kF32 ? 2u : 1u, (uint32_t)n_tile);
@@ -336,14 +338,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         for (int t = blockIdx.x; t < p.total && ok; t += gridDim.x) {
           const Item it = decode<SPLIT>(p, t);
           const int nt = it.nt;
-          if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u)) {
+          if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, lim)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t d = tmem + (uint32_t)acc * p.acc_stride;
           for (int s = it.s0; s < it.s1; s++) {
-            if (!mbar_wait(&a_ready[gs], gph) || (!p.b_res && !mbar_wait(&g_full[gs], gph))) {
+            if (!mbar_wait(&a_ready[gs], gph, lim) || (!p.b_res && !mbar_wait(&g_full[gs], gph, lim))) {
               ok = false;
               break;
             }
@@ -376,8 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
           if ((int)(q % p.ng) != grp) continue;
           const int hs = (int)(q % p.sh), gs = (int)(q % p.sg);
           const uint32_t hph = (uint32_t)((q / p.sh) & 1), gph = (uint32_t)((q / p.sg) & 1);
-          if (!__all_sync(0xffffffffu, mbar_wait(&h_full[hs], hph)) ||
-              !__all_sync(0xffffffffu, mbar_wait(&g_empty[gs], gph ^ 1u))) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&h_full[hs], hph, lim)) ||
+              !__all_sync(0xffffffffu, mbar_wait(&g_empty[gs], gph ^ 1u, lim))) {
             ok = false;
             break;
           }
@@ -435,8 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         uint64_t *full = &acc_full[acc];
         const uint32_t ph = acc_phase;
         if (!epilogue_rows<T, 0>(ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), lane_base, 0,
-                                 n_tile, it.nt * n_tile, blk, pix_of(it), [full, ph]() {
-                                   const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph));
+                                 n_tile, it.nt * n_tile, blk, pix_of(it), [full, ph, lim]() {
+                                   const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph, lim));
                                    tc_fence_after();
                                    return w;
                                  })) {
@@ -466,8 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         if (!epilogue_tma<T>(
                 ea, tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16), row, n_tile, n0, m, bufs, slice,
                 elected, bar_id, kEpiW * 32,
-                [full, ph, bar_id]() {
-                  const bool w = bar_and(bar_id, kEpiW * 32, mbar_wait(full, ph));
+                [full, ph, bar_id, lim]() {
+                  const bool w = bar_and(bar_id, kEpiW * 32, mbar_wait(full, ph, lim));
                   tc_fence_after();
                   return w;
                 },
@@ -491,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
       const size_t tile_elems = (size_t)kTileM * n_tile;
       for (int t = t_first; t < p.total && ok; t += t_step) {
         const Item it = decode<SPLIT>(p, t);
-        const bool w = bar_and(1, kEpiW * 32, mbar_wait(&acc_full[acc], acc_phase));
+        const bool w = bar_and(1, kEpiW * 32, mbar_wait(&acc_full[acc], acc_phase, lim));
         tc_fence_after();
         if (!w) {
           ok = false;
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     }
   }
 
-  if (!ok && p.err) atomicExch(p.err, 1);
+  if (!ok) report_gave_up(p.err);
   __syncwarp();  // lanes that idled while lane 0 worked rejoin before the block barrier
   tc_fence_before();
   __syncthreads();

@@ -45,6 +45,7 @@ struct Params {
   const uint8_t *wimg;  // [n tile][slab] images of b_bytes
   EpiArgs epi;
   int *err;
+  long long wait;  // cycles a pipeline wait may take before the role gives up
   long M;
   int n_tiles, m_tiles, slabs, stages;
   uint32_t acc_stride, tmem_cols, b_bytes, bias_bytes;
@@ -162,7 +163,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
   uint64_t *acc_empty = acc_full + 2;
   uint64_t *c_full = acc_empty + 2;
   uint64_t *c_empty = c_full + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(c_empty + 2);
+  uint64_t *drain = c_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tile = p.epi.n_tile;
@@ -178,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       mbar_init(&c_full[a], kNumConv);
       mbar_init(&c_empty[a], kEpiWarps);
     }
+    mbar_init(drain, 1);
     fence_barrier_init();
   }
   if (tid == 0) pdl_trigger();
@@ -189,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
   const uint32_t tmem = *tmem_slot;
   const int total = p.m_tiles * p.n_tiles;
   bool ok = true;
+  const long long lim = p.wait;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -196,10 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       pdl_wait();  // the A tiles are the previous kernel's output
       int stage = 0;
       uint32_t phase = 0;
+      long issued = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const int mt = t / p.n_tiles, nt = t % p.n_tiles;
         for (int s = 0; s < p.slabs; s++) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, lim)) {
             ok = false;
             break;
           }
@@ -208,9 +213,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
           tma_load_2d(smem_u32(st), &tmap_a, s * kSlabC, mt * kTileM, &full[stage]);
           bulk_load(smem_u32(st + kTerms * kAImage), p.wimg + ((size_t)nt * p.slabs + s) * p.b_bytes, p.b_bytes,
                     &full[stage]);
+          issued++;
           if (++stage == S) stage = 0, phase ^= 1u;
         }
       }
+      // every copy issued above lands before the CTA may leave (a consumer
+      // that gave up leaves its stages unread)
+      for (long i = issued > S ? issued - S : 0; i < issued; i++)
+        ok = mbar_wait(&full[i % S], (uint32_t)((i / S) & 1)) && ok;
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -220,14 +230,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       const uint32_t idesc = instr_desc(kF32 ? 2u : 1u, (uint32_t)n_tile);
       const uint32_t b_img = (uint32_t)n_tile * 128u;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u)) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, lim)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)acc * p.acc_stride;
         for (int s = 0; s < p.slabs; s++) {
-          if (!mbar_wait(&full[stage], phase) || (kF32 && !mbar_wait(&lo_rdy[stage], phase))) {
+          if (!mbar_wait(&full[stage], phase, lim) || (kF32 && !mbar_wait(&lo_rdy[stage], phase, lim))) {
             ok = false;
             break;
           }
@@ -242,6 +252,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
         mma_commit(&acc_full[acc]);
         if (++acc == 2) acc = 0, acc_phase ^= 1u;
       }
+      // no MMA of this thread is in flight once `drain` completes
+      mma_commit(drain);
+      if (!mbar_wait(drain, 0)) ok = false;
     }
   } else if (warp < kEpiWarp0) {
     // ------------------------------------------ TF32 split, lateral coarse term
@@ -253,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       if (kF32) {
         for (int s = 0; s < p.slabs; s++) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase))) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, lim))) {
             ok = false;
             break;
           }
@@ -275,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       }
       if (ring) {
         // (8-row run, 4-column group) items, ahead of the epilogue
-        if (!__all_sync(0xffffffffu, mbar_wait(&c_empty[cst], cph ^ 1u))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&c_empty[cst], cph ^ 1u, lim))) {
           ok = false;
           break;
         }
@@ -316,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       const uint32_t tacc = tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16);
       const float *cs_row = nullptr;
       if (MODE == 2 && p.cs_stages > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&c_full[cst], cph))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&c_full[cst], cph, lim))) {
           ok = false;
           break;
         }
@@ -324,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
         ea.cs_n0 = nt * n_tile;
         cs_row = ea.cs + (lane_base + lane) * p.cs_ld;
       }
-      auto ready = [full, ph]() {
-        const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph));
+      auto ready = [full, ph, lim]() {
+        const bool w = __all_sync(0xffffffffu, mbar_wait(full, ph, lim));
         tc_fence_after();
         return w;
       };
@@ -364,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     if (lane == 0) bulk_wait_all();  // this warp's stores are written before the CTA leaves
   }
 
-  if (!ok && p.err) atomicExch(p.err, 1);
+  if (!ok) report_gave_up(p.err);
   __syncwarp();  // lanes that idled while lane 0 worked rejoin before the block barrier
   tc_fence_before();
   __syncthreads();
@@ -456,6 +469,7 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
 
   tcp::Params p;
   p.wimg = wimg, p.err = err, p.M = op.M;
+  p.wait = op.wait_cycles > 0 ? op.wait_cycles : tcx::kWaitCycles;
   p.epi.bias = op.bias, p.epi.res = op.res, p.epi.coarse = op.coarse, p.epi.dst = op.dst;
   p.epi.N = op.N, p.epi.act = op.act, p.epi.OH = op.OH, p.epi.OW = op.OW, p.epi.n_tile = plan.n_tile;
   p.n_tiles = plan.n_tiles, p.slabs = plan.slabs;
@@ -471,7 +485,7 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   p.cs_ld = plan.n_tile + (plan.n_tile % 32 == 0 ? 16 : 0);
   // deepest coarse ring (2, 1 or none) that leaves at least 3 (else 2) A/B stages
   const size_t cs_stage = (size_t)tcx::kTileM * p.cs_ld * 4;
-  const size_t fixed0 = 1024 + tcp::kEpiPw + p.bias_bytes + 8 * (3 * 8 + 8) + 16;
+  const size_t fixed0 = 1024 + tcp::kEpiPw + p.bias_bytes + 8 * (3 * 8 + 9) + 16;
   p.cs_stages = 0;
   if (op.mode == 2)
     for (int want_ab = 3; want_ab >= 2 && !p.cs_stages; want_ab--)
@@ -486,7 +500,7 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   if (stages > 6) stages = 6;
   if (stages < 2) return cudaErrorInvalidValue;
   p.stages = stages;
-  const size_t smem = stages * stage + 1024 + tcp::kEpiPw + p.bias_bytes + p.cs_bytes + 8 * (3 * stages + 8) + 16;
+  const size_t smem = stages * stage + 1024 + tcp::kEpiPw + p.bias_bytes + p.cs_bytes + 8 * (3 * stages + 9) + 16;
   if (T == F32) return op.mode == 0 ? launch<float, 0>(map, map_out, p, smem, st) : launch<float, 2>(map, map_out, p, smem, st);
   return op.mode == 0 ? launch<__nv_bfloat16, 0>(map, map_out, p, smem, st) : launch<__nv_bfloat16, 2>(map, map_out, p, smem, st);
 }

@@ -101,11 +101,15 @@ SIGNATURES = {
     "illumina_forward": (_S, [_V, _V, C.c_int, C.c_int, _V, _V, _V]),
     "illumina_model_record": (_S, [_V, _V, C.c_int, _V]),
     "illumina_model_swap_history": (_S, [_V]),
+    "illumina_model_sync": (_S, [_V]),
+    "illumina_model_set_wait_limit": (_S, [_V, C.c_longlong]),
     "illumina_model_output_parity": (C.c_int, [_V]),
     "illumina_model_fresh_parity": (C.c_int, [_V]),
     "illumina_model_depth_slot": (_S, [_V, C.c_int, C.POINTER(C.c_void_p)]),
     "illumina_model_debug_tensor": (_S, [_V, C.c_char_p, _V, C.c_size_t, C.POINTER(C.c_int),
                                          C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "illumina_model_debug_tensor_frame": (_S, [_V, C.c_char_p, C.c_int, _V, C.c_size_t, C.POINTER(C.c_int),
+                                               C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "illumina_model_stats": (_S, [_V, C.POINTER(Stats)]),
     "illumina_model_profile": (_S, [_V, _V, C.c_int, C.c_int, C.c_int, _V, C.c_int]),
     "illumina_set_op_engine": (_S, [C.c_int]),

@@ -123,6 +123,15 @@ class DepthModel:
             frame = np.ascontiguousarray(frame, np.float32)
         check(lib().illumina_model_record(self._h, ptr(frame), layout, stream_handle(stream)))
 
+    def sync(self):
+        """Waits for this model's queued work; raises IlluminaError (status TIMEOUT) when a
+        kernel gave up a bounded wait since the last check."""
+        check(lib().illumina_model_sync(self._h))
+
+    def setWaitLimit(self, cycles: int):
+        """Cycles a tensor-core pipeline wait may take before the kernel gives up (0 = default)."""
+        check(lib().illumina_model_set_wait_limit(self._h, int(cycles)))
+
     def swapHistory(self):
         check(lib().illumina_model_swap_history(self._h))
 
@@ -170,15 +179,16 @@ class DepthModel:
         check(lib().illumina_model_profile(self._h, ptr(frames), n, layout, reps, out.ctypes.data, out.size))
         return {op.name: float(t) for op, t in zip(self.arch.ops, out)}
 
-    def debugTensor(self, name: str):
-        """debugTensor (runner.ts:466-476): (frame-0 data [h, w, c] float32 numpy, liveAtEnd) or None."""
+    def debugTensor(self, name: str, frame: int = 0):
+        """debugTensor (runner.ts:466-476): (data [h, w, c] float32 numpy of batch frame `frame` of the
+        last forward, liveAtEnd) or None."""
         if name not in self.arch.tensors or name == "depth":
             return None
         s = self.arch.tensors[name]
         out = np.empty((s.h, s.w, s.c), np.float32)
         h, w, c, live = C.c_int(), C.c_int(), C.c_int(), C.c_int()
-        check(lib().illumina_model_debug_tensor(self._h, name.encode(), out.ctypes.data, out.size, C.byref(h),
-                                                C.byref(w), C.byref(c), C.byref(live)))
+        check(lib().illumina_model_debug_tensor_frame(self._h, name.encode(), int(frame), out.ctypes.data, out.size,
+                                                      C.byref(h), C.byref(w), C.byref(c), C.byref(live)))
         return out, bool(live.value)
 
     def destroy(self):

@@ -153,7 +153,13 @@ illumina_status illumina_model_set_temporal(illumina_model *model, float base_al
  * bilateralUp. `disparity` receives n x S x S float32 (the `depth` texture's
  * x channel); `depth_low` (nullable) receives n x S/2 x S/2 float32 (head
  * output, channel 0). The launch sequence is captured once per distinct
- * (n, pointers) and replayed as a CUDA graph. */
+ * (n, pointers) and replayed as a CUDA graph.
+ * ILLUMINA_TIMEOUT: a tensor-core kernel gave up a bounded wait (its outputs
+ * are undefined; the model stays usable). A call with a host buffer
+ * synchronises and reports its own kernels; a call on device buffers only
+ * queues them, and a give-up is reported by the model's next forward, record
+ * or illumina_model_sync (the reference's device errors are asynchronous
+ * too: uncaptured-error events, src/main.ts). */
 illumina_status illumina_forward(illumina_model *model, const float *frames, int n, int frame_layout,
                                  float *disparity, float *depth_low, void *stream);
 
@@ -163,6 +169,18 @@ illumina_status illumina_forward(illumina_model *model, const float *frames, int
  * texture (stabilised, raw, change, 1) into slot outputParity(). */
 illumina_status illumina_model_record(illumina_model *model, const float *frame, int frame_layout,
                                       void *stream);
+/* Waits for the work queued on the model's stream and reports a kernel that
+ * gave up a bounded wait as ILLUMINA_TIMEOUT -- the synchronous check of a
+ * device-buffer forward (the reference's `device.queue.onSubmittedWorkDone()`
+ * plus its error scope, src/model/runner.ts:425-434). */
+illumina_status illumina_model_sync(illumina_model *model);
+/* Cycles a tensor-core pipeline wait may take before the kernel gives up and
+ * reports ILLUMINA_TIMEOUT (0 = the default, ~1 s; the waits with which a
+ * kernel that gave up drains its own copies and MMAs keep the default). A
+ * fault-handling hook with no reference counterpart: a small limit makes a
+ * forward's waits give up so that the error path can be exercised. Drops the
+ * captured graphs. */
+illumina_status illumina_model_set_wait_limit(illumina_model *model, long long cycles);
 /* DepthModel.swapHistory / outputParity / freshParity (runner.ts:450-454). */
 illumina_status illumina_model_swap_history(illumina_model *model);
 int illumina_model_output_parity(const illumina_model *model);
@@ -177,6 +195,12 @@ illumina_status illumina_model_depth_slot(illumina_model *model, int index, cons
  * after a full forward (live_at_end = 0 when a later tensor reused it). */
 illumina_status illumina_model_debug_tensor(illumina_model *model, const char *name, float *out,
                                             size_t cap, int *h, int *w, int *c, int *live_at_end);
+
+/* DepthModel.debugTensor (runner.ts:466-476) for frame `frame` (0 <= frame <
+ * max_batch) of the last batched forward; illumina_model_debug_tensor is this
+ * call with frame 0. INVALID_ARG for a frame outside the model's batch. */
+illumina_status illumina_model_debug_tensor_frame(illumina_model *model, const char *name, int frame, float *out,
+                                                  size_t cap, int *h, int *w, int *c, int *live_at_end);
 
 /* DepthModel.stats (runner.ts:95-101, :425-434). */
 typedef struct illumina_stats {
@@ -244,7 +268,9 @@ illumina_status illumina_op_dwpw(const float *src, int in_h, int in_w, int in_c,
  * array's device address (cudaGetSymbolAddress) with that device current; make
  * that first call before any stream capture. All calls share the array: calls
  * whose GPU work overlaps (other streams or host threads on the same device)
- * race. Arguments and result are those of illumina_op_dwpw. */
+ * race. Arguments and result are those of illumina_op_dwpw; the work runs on
+ * the SIMT engine whatever illumina_set_op_engine selected for the calling
+ * thread (the tensor engine's weight images would need an allocation). */
 #define ILLUMINA_NOALLOC_DW_MAX_FLOATS 65536
 illumina_status illumina_op_dwpw_noalloc(const float *src, int in_h, int in_w, int in_c, const float *dw_w,
                                          const float *dw_b, int mid_act, const float *pw_w, const float *pw_b,

@@ -56,6 +56,11 @@ def declare(lib):
         "or_scene_render": (None, [F, C.c_int, C.c_int, F, U8, F]),
         "or_evaluate_depth": (None, [F, C.c_int, F, C.c_int, C.c_int, D]),
         "or_resize_bilinear": (None, [F, C.c_int, C.c_int, F, C.c_int, C.c_int]),
+        "or_blob_frame": (None, [C.c_uint32, C.c_int, F]),
+        "or_det_exp": (C.c_double, [C.c_double]),
+        "or_det_log": (C.c_double, [C.c_double]),
+        "or_det_cos2pi": (C.c_double, [C.c_double]),
+        "or_det_sincos": (None, [C.c_double, D, D]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

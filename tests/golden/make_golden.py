@@ -10,7 +10,7 @@ read-only from a checkout of the reference repository:
 
 Run once in a container that has the reference checkout (the GPU box does not):
 
-    python -B tests/golden/make_golden.py --reference /root/reference
+    python -B tests/golden/make_golden.py --reference <path of the reference checkout>
 
 Outputs (committed, a few hundred KB):
   arch.json        layer table, costs and weight specs at 64 and 448

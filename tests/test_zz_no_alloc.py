@@ -65,6 +65,28 @@ def test_noalloc_matches_allocating_entry_point_on_consecutive_calls(torch):
         assert worst == [], (cid, worst)
 
 
+def test_noalloc_runs_simt_whatever_engine_the_thread_selected(torch):
+    """With the tensor engine selected for the thread, illumina_op_dwpw runs
+    tcgen05 while the no-alloc variant still runs the SIMT kernel: both match
+    the oracle within the kernel tolerance and each other within it too."""
+    from illumina import _lib
+    lib = _lib.lib()
+    case = {c["id"]: c for c in cases.all_cases()}["s_dwpw10"]
+    data = cases.draw(case)
+    lib.illumina_set_op_engine(_lib.ENGINE["tensor"])
+    try:
+        got = _call(lib.illumina_op_dwpw_noalloc, torch, case, data)
+        tc = _call(lib.illumina_op_dwpw, torch, case, data)
+    finally:
+        lib.illumina_set_op_engine(_lib.ENGINE["simt"])
+    want = cases.oracle_output(case, data)
+    for out in (got, tc):
+        _, _, worst = compare(out, want, *case["tol"])
+        assert worst == [], worst
+    _, _, worst = compare(got, tc, *case["tol"])
+    assert worst == []
+
+
 def test_noalloc_rejects_weights_beyond_the_fixed_scratch(torch):
     from illumina import _lib
     lib = _lib.lib()
