@@ -144,6 +144,8 @@ cudaError_t copy_round(const float *w, long n, float *out, int round_bf16, cudaS
 
 // Expand a 1-channel map to 4 channels (debugTensor of depth_low).
 cudaError_t expand4(const float *src, long n, float *dst4, cudaStream_t st);
+// Bilateral guide of a given fp32 network input (n*S*S x 4): its channel 3.
+cudaError_t input_luma(const float *input, long px, float *luma, cudaStream_t st);
 // Convert storage T -> f32.
 cudaError_t to_f32(int T, const void *src, long n, float *dst, cudaStream_t st);
 

@@ -1039,6 +1039,19 @@ cudaError_t to_f32(int T, const void *src, long n, float *dst, cudaStream_t st) 
   return cudaGetLastError();
 }
 
+// Luminance guide of a given network input: its channel 3 (the unnormalised
+// luminance the preprocess stores there, equal to the guide it writes).
+__global__ void k_input_luma(const float4 *__restrict__ input, long px, float *__restrict__ luma) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < px) luma[i] = input[i].w;
+}
+
+cudaError_t input_luma(const float *input, long px, float *luma, cudaStream_t st) {
+  if (px <= 0) return cudaSuccess;
+  k_input_luma<<<blocks_for(px, 256), 256, 0, st>>>(reinterpret_cast<const float4 *>(input), px, luma);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------------------
 // synthetic frames and checksums
 // ---------------------------------------------------------------------------

@@ -290,9 +290,12 @@ cudaGraphNode_t last_captured_node(cudaStream_t st) {
   return deps[0];
 }
 
+// from_input: the network input is already in the arena (the preprocess
+// output, e.g. from an activation bundle): preprocess is skipped and the stem
+// runs as its own conv launch.
 int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, float *disp, float *low_out,
                     const float *history, float *out_tex, const std::vector<cudaEvent_t> *marks = nullptr,
-                    CaptureNodes *nodes = nullptr) {
+                    CaptureNodes *nodes = nullptr, bool from_input = false) {
   const Architecture &a = m.arch;
   const int S = a.input_size;
   int launches = 0;
@@ -307,7 +310,8 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
   for (size_t i = 0; i < a.ops.size(); i++) {
     const Op &op = a.ops[i];
     if (marks) cuda_check(cudaEventRecord((*marks)[i], st), "profile event");
-    if ((int)i == m.stem_fused_op) continue;  // ran inside the preprocess launch
+    if (from_input && op.kind == OpKind::Preprocess) continue;
+    if ((int)i == m.stem_fused_op && !from_input) continue;  // ran inside the preprocess launch
     const OpWeights &w = m.opw[i];
     switch (op.kind) {
       case OpKind::Preprocess:
@@ -1011,6 +1015,35 @@ illumina_status illumina_forward(illumina_model *m, const float *frames, int n, 
   ILL_CATCH
 }
 
+illumina_status illumina_forward_input(illumina_model *m, const float *input, int n, float *disparity,
+                                       float *depth_low) {
+  ILL_TRY
+  require(m && input, "forwardInput: null argument");
+  require(m->T == gpu::F32, "forwardInput: the network input is given in fp32; use an fp32 model");
+  require(n >= 1 && n <= m->opts.max_batch, "forwardInput: batch " + std::to_string(n) + " outside [1, " +
+                                                std::to_string(m->opts.max_batch) + "]");
+  cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+  check_timeout(*m, "in an earlier call on this model");
+  const int S = m->arch.input_size;
+  const size_t px = (size_t)n * S * S;
+  float *in = (float *)m->tensor("input");
+  cuda_check(cudaMemcpyAsync(in, input, sizeof(float) * 4 * px, cudaMemcpyDefault, m->stream), "input copy");
+  // the bilateral guide is the input's unnormalised luminance (channel 3)
+  cuda_check(gpu::input_luma(in, (long)px, m->d_luma, m->stream), "guide");
+  enqueue_forward(*m, n, nullptr, ILLUMINA_FRAME_RGB_PLANAR, m->d_stage_out, m->d_stage_low, nullptr, nullptr,
+                  nullptr, nullptr, true);
+  if (disparity)
+    cuda_check(cudaMemcpyAsync(disparity, m->d_stage_out, sizeof(float) * px, cudaMemcpyDefault, m->stream),
+               "disparity copy");
+  if (depth_low)
+    cuda_check(cudaMemcpyAsync(depth_low, m->d_stage_low, sizeof(float) * px / 4, cudaMemcpyDefault, m->stream),
+               "depth_low copy");
+  cuda_check(cudaStreamSynchronize(m->stream), "synchronize");
+  check_timeout(*m, "in this call");
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
 illumina_status illumina_model_record(illumina_model *m, const float *frame, int layout, void *stream) {
   ILL_TRY
   require(m, "record: null model");
@@ -1064,12 +1097,32 @@ illumina_status illumina_model_debug_tensor_frame(illumina_model *m, const char 
   ILL_TRY
   require(m && name, "debugTensor: null argument");
   std::string n(name);
+  require(frame >= 0 && frame < m->opts.max_batch,
+          "debugTensor: frame " + std::to_string(frame) + " outside [0, " + std::to_string(m->opts.max_batch) + ")");
+  if (n == "scene_color") {
+    // the preprocess's second output (linear exposed colour, alpha 1), kept
+    // only by a keep-intermediates model
+    const int S = m->arch.input_size;
+    require(m->d_scene != nullptr, "debugTensor: scene_color is kept only by a keepIntermediates model");
+    if (h) *h = S;
+    if (w) *w = S;
+    if (c) *c = 4;
+    if (live_at_end) *live_at_end = 1;
+    if (!out) return ILLUMINA_OK;
+    const size_t count = (size_t)4 * S * S;
+    require(cap >= count, "debugTensor: output holds " + std::to_string(cap) + " floats, tensor needs " +
+                              std::to_string(count));
+    cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+    cuda_check(cudaMemcpyAsync(out, m->d_scene + (size_t)frame * count, sizeof(float) * count, cudaMemcpyDefault,
+                               m->stream),
+               "debugTensor copy");
+    cuda_check(cudaStreamSynchronize(m->stream), "debugTensor copy");
+    return ILLUMINA_OK;
+  }
   auto ts = m->arch.tensors.find(n);
   auto as = m->plan.assignment.find(n);
   if (ts == m->arch.tensors.end() || as == m->plan.assignment.end())
     throw Error(ILLUMINA_INVALID_ARG, "debugTensor: unknown tensor " + n);
-  require(frame >= 0 && frame < m->opts.max_batch,
-          "debugTensor: frame " + std::to_string(frame) + " outside [0, " + std::to_string(m->opts.max_batch) + ")");
   const TensorShape &s = ts->second;
   if (h) *h = s.h;
   if (w) *w = s.w;

@@ -12,12 +12,15 @@ The names mirror the reference's TypeScript API surface for the hot path:
   frame     renderFrame -> FrameResult                               (src/engine/frame.ts)
   scene     createProceduralScene, renderScenes, evaluateDepth       (src/scene/procedural.ts, metrics.ts)
   ops       per-kernel entry points                                  (src/model/kernels/*.ts)
+  bundle    readBundle, writeBundle, dumpForward (ntb/1)             (scripts/ref-forward.ts)
+  ref_forward  the ref-forward CLI on the CUDA path: python -m illumina.ref_forward
 
 Everything computes in libillumina.so (CUDA for sm_100a); there is no CPU path.
 """
 from ._lib import IlluminaError, lib  # noqa: F401
 from .arch import Architecture, TensorShape, buildArchitecture, costOf, formatCost, weightSpecs  # noqa: F401
 from .arena import opInputs, planArena, validateArena  # noqa: F401
+from .bundle import dumpForward, readBundle, writeBundle  # noqa: F401
 from .frame import FrameResult, renderFrame  # noqa: F401
 from .lighting import (DEFAULT_SETTINGS, MAX_LIGHTS, LightDescription, LightKind, Renderer,  # noqa: F401
                        ShadingSettings, createRenderer, packLights)

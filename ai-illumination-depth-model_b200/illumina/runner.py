@@ -88,6 +88,23 @@ class DepthModel:
                                      stream_handle(stream)))
         return disparity
 
+    def forwardInput(self, inputs, disparity=None, depthLow=None):
+        """forwardReference from given network inputs (ref-forward.ts with an "input" bundle):
+        [n, S, S, 4] float32 channels-last preprocess outputs. Synchronous; returns the disparity
+        [n, S, S] (numpy unless `disparity` is given). fp32 models only."""
+        S = self.arch.inputSize
+        x = inputs if _is_torch(inputs) else np.ascontiguousarray(inputs, np.float32)
+        shape = tuple(x.shape)
+        if len(shape) == 3:
+            shape = (1,) + shape
+        if shape[1:] != (S, S, 4):
+            raise ValueError(f"inputs must be [n,{S},{S},4], got {list(x.shape)}")
+        n = shape[0]
+        if disparity is None:
+            disparity = np.empty((n, S, S), np.float32)
+        check(lib().illumina_forward_input(self._h, ptr(x), n, ptr(disparity), ptr(depthLow)))
+        return disparity
+
     def sampleSource(self, rgba8, uvScale=None, uvOffset=None, mirror: bool = False, frames=None, stream=None):
         """The source-texture read of makePreprocess (io.ts:64-118): n 8-bit RGBA
         images [n, h, w, 4] (CUDA uint8 tensor, any size) sampled at the network
@@ -181,11 +198,16 @@ class DepthModel:
 
     def debugTensor(self, name: str, frame: int = 0):
         """debugTensor (runner.ts:466-476): (data [h, w, c] float32 numpy of batch frame `frame` of the
-        last forward, liveAtEnd) or None."""
-        if name not in self.arch.tensors or name == "depth":
+        last forward, liveAtEnd) or None. "scene_color" (the preprocess's linear colour) is kept by a
+        keepIntermediates model."""
+        if name == "scene_color":
+            S = self.arch.inputSize
+            out = np.empty((S, S, 4), np.float32)
+        elif name not in self.arch.tensors or name == "depth":
             return None
-        s = self.arch.tensors[name]
-        out = np.empty((s.h, s.w, s.c), np.float32)
+        else:
+            s = self.arch.tensors[name]
+            out = np.empty((s.h, s.w, s.c), np.float32)
         h, w, c, live = C.c_int(), C.c_int(), C.c_int(), C.c_int()
         check(lib().illumina_model_debug_tensor_frame(self._h, name.encode(), int(frame), out.ctypes.data, out.size,
                                                       C.byref(h), C.byref(w), C.byref(c), C.byref(live)))

@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip batch-1 latency and bf16 lines")
+    ap.add_argument("--only", default=None, choices=["relight", "sweep", "streaming", "bf16"],
+                    help="run just one extra measurement on rank 0 and print it (for profiling)")
     return ap.parse_args()
 
 
@@ -86,6 +88,16 @@ class RankGroup:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def all_gather(self, t):
+        """Rank-ordered concatenation of every rank's equal-sized tensor `t`."""
+        if not self.pg:
+            return t
+        import torch
+        import torch.distributed as dist
+        parts = [torch.empty_like(t) for _ in range(self.world)]
+        dist.all_gather(parts, t)
+        return torch.cat(parts)
+
     def close(self):
         if self.pg:
             import torch.distributed as dist
@@ -97,6 +109,20 @@ def frame_seed_base(rank: int, batch: int) -> int:
     """Rank r generates frames with seeds [r*batch, (r+1)*batch): disjoint
     frame ranges, so N ranks process N*batch distinct frames (weak scaling)."""
     return rank * batch
+
+
+def shard(total: int, rank: int, world: int):
+    """Contiguous block of frame indexes [first, first + count) of `rank`."""
+    per = total // world
+    return rank * per, per
+
+
+def checksum_digest(sums) -> str:
+    """Digest of the per-frame u64 disparity checksums in frame order."""
+    import hashlib
+
+    import numpy as np
+    return hashlib.sha256(np.ascontiguousarray(sums, dtype=np.uint64).tobytes()).hexdigest()[:16]
 
 
 def aggregate_frames_per_s(world: int, batch: int, steps: int, ms_max: float) -> float:
@@ -231,23 +257,33 @@ def load_traffic():
 # CPU oracle timing (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 
+_CPU_FRAMES = {}
+
+
+def cpu_frames(count: int, threads: int):
+    """`count` blob frames (seeds 0..count-1, the device generator's frames of
+    rank 0), generated once across the thread pool."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import frames as OF
+    missing = [i for i in range(count) if i not in _CPU_FRAMES]
+    if missing:
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            for i, f in zip(missing, ex.map(lambda k: OF.blob_frame(k, SIZE), missing)):
+                _CPU_FRAMES[i] = f.ravel()
+    return [_CPU_FRAMES[i] for i in range(count)]
+
+
 def cpu_oracle_frames_per_s(n_frames: int, threads: int):
     """Times the oracle port of the reference CPU forward (preprocess -> 38 convs -> head ->
-    bilateralUp, double accumulation) on `n_frames` 448 blob-frame-shaped inputs across
-    `threads` host threads. Returns (frames/s, seconds)."""
-    import numpy as np
+    bilateralUp, double accumulation) on `n_frames` 448 blob frames (the benchmark's input)
+    across `threads` host threads. Returns (frames/s, seconds)."""
     from concurrent.futures import ThreadPoolExecutor
     from oracle import arch as OA
-    from oracle import lib as olib
     from oracle import reference as R
     from oracle import weights as OW
     a = OA.build_architecture(SIZE)
     w = OW.synthesize_weights(a, 0)
-    frames = []
-    for i in range(min(n_frames, threads)):
-        f = np.empty(3 * SIZE * SIZE, np.float32)
-        olib().or_uniform_frame(i, f.size, f.ctypes.data_as(C.POINTER(C.c_float)))
-        frames.append(f)
+    frames = cpu_frames(min(n_frames, threads), threads)
 
     def one(i):
         R.forward_frame(a, w, frames[i % len(frames)])
@@ -281,7 +317,7 @@ def run_reference(args, rank, world):
         total_t += dt
         total_f += per_step
     value = total_f / total_t
-    sample = f"{per_step} frames of 3x448x448 per step ({threads} threads, one frame each)"
+    sample = f"{per_step} blob frames of 3x448x448 per step ({threads} threads, one frame each)"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total_t / max(1, args.steps),
@@ -303,6 +339,29 @@ def run_reference(args, rank, world):
 
 RELIGHT_W, RELIGHT_H = 1920, 1080
 RELIGHT_STEPS = (16, 6, 4, 12)  # contact, AO directions x steps (24 samples), volumetric per light (x4 = 48)
+
+
+def shade_roofline(shade_ms):
+    """The shading kernel against the FP32 CUDA-core rate: algorithmic FLOPs per
+    pixel from the op-counting build of the shading restatement (committed in
+    profiles/shade_flops_1080p.json, benchmark step counts) over the measured
+    time; peak = SMs x 128 FP32 lanes x 2 (FMA) x the measured maximum SM clock."""
+    import torch
+    try:
+        with open(os.path.join(REPO, "profiles", "shade_flops_1080p.json")) as f:
+            fpp = float(json.load(f)["benchmark"]["flops_per_pixel"])
+    except Exception:  # noqa: BLE001
+        return None
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            mhz, src = float(json.load(f)["sm_max_mhz"]), "MEASURED_PEAKS.json sm_max_mhz"
+    except Exception:  # noqa: BLE001
+        mhz, src = 1965.0, "clocks.max.sm 1965 MHz"
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    peak = sms * 128 * 2 * mhz * 1e6 / 1e12
+    achieved = fpp * RELIGHT_W * RELIGHT_H / (shade_ms / 1000.0) / 1e12
+    return {"bound": "fp32", "flops_per_pixel": fpp, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "peak_source": f"{sms} SMs x 128 x 2 x {mhz:.0f} MHz ({src})"}
 
 
 def depth_relight_frame(model, frames, ring, stream, ev0, ev1, reps=60):
@@ -353,6 +412,7 @@ def depth_relight_frame(model, frames, ring, stream, ev0, ev1, reps=60):
     shade_ms = ev0.elapsed_time(ev1) / reps
     return {"ms_per_frame": frame_ms, "shade_ms": shade_ms, "resolution": f"{RELIGHT_W}x{RELIGHT_H}",
             "mpix_per_s_shade": RELIGHT_W * RELIGHT_H / shade_ms / 1e3,
+            "shade_roofline": shade_roofline(shade_ms),
             "steps": {"contact": RELIGHT_STEPS[0], "ao_samples": RELIGHT_STEPS[1] * RELIGHT_STEPS[2],
                       "volumetric_per_light": RELIGHT_STEPS[3], "lights": 4},
             "input": "uniform [0,1] 448 frame, batch 1; albedo = the frame's RGB (bilinear)"}
@@ -423,6 +483,98 @@ def source_sampling(model, stream, ev0, ev1, batch=64, reps=10):
     ms = ev0.elapsed_time(ev1) / reps
     return {"us_per_frame": 1000.0 * ms / batch, "ms_per_launch": ms, "batch": batch,
             "source": f"{w}x{h} RGBA8, centre crop, bilinear clamp-to-edge", "output": "3x448x448 f32 planar"}
+
+
+def batch_sweep(model, frames, disp, stream, ev0, ev1, batches=(1, 8, 64, 256)):
+    """Latency and frames/s of one forward at each batch size (device-resident
+    blob frames; batch b takes consecutive slices of the 256 generated frames
+    in turn, so small batches do not re-read L2-resident inputs)."""
+    import torch
+    out = []
+    n = frames.shape[0]
+    for b in batches:
+        if b > n:
+            continue
+        views = [(frames[i:i + b], disp[i:i + b]) for i in range(0, n - b + 1, b)]
+        reps = max(5, min(200, 2048 // b))
+        for k in range(min(len(views), 8) + 3):
+            model.forward(views[k % len(views)][0], disparity=views[k % len(views)][1], stream=stream)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for k in range(reps):
+            model.forward(views[k % len(views)][0], disparity=views[k % len(views)][1], stream=stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / reps
+        out.append({"batch": b, "latency_ms": ms, "frames_per_s": b * 1000.0 / ms, "us_per_frame": 1000.0 * ms / b})
+    return out
+
+
+def streaming_frames(model, rank, world, stream, ranks, total=8192, batch=256):
+    """Box-scale streaming: `total` independent uniform frames (seed n for frame n),
+    sharded across the ranks in contiguous blocks; each rank generates its frames on
+    its device batch by batch, replays the forward graph over batches of `batch` and
+    takes per-frame checksums of the disparity (u64 sum of the fp32 bit patterns
+    weighted by 2j+1, and a double sum). The only cross-rank step is the final
+    gather of the checksums. Returns throughput over the slowest rank's device time,
+    a digest of the 8192 u64 checksums in frame order (identical at every rank
+    count when every GPU computes the same bits), and a spot check in which rank 0
+    recomputes the last rank's last batch itself."""
+    import numpy as np
+    import torch
+    from illumina import _lib
+
+    lib = _lib.lib()
+    f0, per = shard(total, rank, world)
+    frames = torch.empty((batch, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    disp = torch.empty((batch, SIZE, SIZE), dtype=torch.float32, device="cuda")
+    h64 = torch.zeros(per, dtype=torch.int64, device="cuda")
+    fsum = torch.zeros(per, dtype=torch.float64, device="cuda")
+    sh = _lib.stream_handle(stream)
+
+    def one_batch(first, nb, h_out, s_out):
+        _lib.check(lib.illumina_generate_frames(0, first, nb, SIZE, frames.data_ptr(), sh))
+        model.forward(frames[:nb], disparity=disp[:nb], stream=stream)
+        _lib.check(lib.illumina_checksums(disp.data_ptr(), nb, SIZE * SIZE, h_out.data_ptr(), s_out.data_ptr(), sh))
+
+    def run():
+        for b0 in range(0, per, batch):
+            nb = min(batch, per - b0)
+            one_batch(f0 + b0, nb, h64[b0:], fsum[b0:])
+
+    run()  # warm-up: graphs for this batch size
+    torch.cuda.synchronize()
+    ranks.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    ms = ranks.max(e0.elapsed_time(e1))
+    # the final host gather of per-frame checksums (the workload's only collective)
+    gh, gs = ranks.all_gather(h64), ranks.all_gather(fsum)
+    res = None
+    if rank == 0:
+        hosts = gh.cpu().numpy().astype(np.uint64)
+        sums = gs.cpu().numpy()
+        # rank 0 recomputes the last batch of the last rank on its own GPU
+        last = total - min(batch, per)
+        nb = total - last
+        ch = torch.zeros(nb, dtype=torch.int64, device="cuda")
+        cs = torch.zeros(nb, dtype=torch.float64, device="cuda")
+        one_batch(last, nb, ch, cs)
+        torch.cuda.synchronize()
+        spot_ok = bool((ch.cpu().numpy().astype(np.uint64) == hosts[last:]).all())
+        res = {"frames": total, "batch": batch, "frames_per_rank": per, "ms": ms,
+               "frames_per_s": total * 1000.0 / ms,
+               "checksum_digest": checksum_digest(hosts),
+               "disparity_mean": float(sums.sum() / (total * SIZE * SIZE)),
+               "spot_check": {"frames": [last, total - 1], "recomputed_on_rank0_equal": spot_ok},
+               "input": "uniform [0,1] frames, seed n for frame n, generated on each device per batch",
+               "timed": "generate + forward (graph replay) + checksums, device time, max over ranks"}
+    return res
 
 
 def bf16_throughput(local_rank, stream, ev0, ev1, batch=256, reps=5):
@@ -517,8 +669,14 @@ def run_ours(args, rank, local_rank, world):
         e_ms = max_over_ranks(ev0.elapsed_time(ev1))
         e2e = {"value": aggregate_frames_per_s(world, B, e_steps, e_ms), "unit": UNIT,
                "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
-               "steps": e_steps, "path": "illumina_forward (C ABI), pinned host buffers"}
+               "steps": e_steps, "path": "illumina_forward (C ABI), pinned host buffers",
+               "aggregate_pcie_gb_per_s": world * e_steps * (host_in.numel() + host_out.numel()) * 4 / e_ms / 1e6}
         del host_in, host_out
+
+    # ---- box-scale streaming: 8192 seeded frames sharded over the ranks ----
+    streaming = None
+    if not args.no_extras:
+        streaming = streaming_frames(model, rank, world, stream, ranks)
 
     # ---- roofline of the dominant kernel (live CUDA events on the launching stream) ----
     hbm, bf16, peak_src = measured_peaks()
@@ -549,9 +707,12 @@ def run_ours(args, rank, local_rank, world):
                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
                     else "fallback 6.65 TB/s"}
 
-    # ---- extras: batch-1 latency (config 1) ----
+    # ---- extras: batch-1 latency (config 1), the batch sweep (config 2) ----
     extras = {}
+    if streaming is not None:
+        extras["streaming_8192"] = streaming
     if rank == 0 and not args.no_extras:
+        extras["batch_sweep"] = batch_sweep(model, frames, disp, stream, ev0, ev1)
         ring = 64  # 64 x 2.4 MB inputs > L2, so inputs are not cached between iterations
         b1_frames = torch.empty((ring, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
         _lib.check(_lib.lib().illumina_generate_frames(0, 0, ring, SIZE, b1_frames.data_ptr(), None))
@@ -581,7 +742,7 @@ def run_ours(args, rank, local_rank, world):
         n = threads * 2
         fps, dt = cpu_oracle_frames_per_s(n, threads)
         cpu = {"value": fps, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{n} frames of 3x448x448 ({dt:.1f} s over {threads} threads); oracle port of "
+               "sample": f"{n} blob frames of 3x448x448 ({dt:.1f} s over {threads} threads); oracle port of "
                          "src/model/reference.ts (double accumulation, f32 storage) + bilateralUp"}
 
     model.destroy()
@@ -604,11 +765,46 @@ def run_ours(args, rank, local_rank, world):
     return 0
 
 
+def run_only(args, local_rank):
+    """One extra measurement alone (a small command to profile one kernel)."""
+    import torch
+
+    import illumina
+    from illumina import _lib
+
+    torch.cuda.set_device(local_rank)
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.only == "bf16":
+        print(json.dumps({"bf16": bf16_throughput(local_rank, stream, ev0, ev1, batch=args.batch, reps=args.steps)}))
+        return 0
+    model = illumina.createDepthModel(illumina.buildArchitecture(SIZE), synthSeed=0, maxBatch=args.batch,
+                                      precision=args.precision, device=local_rank)
+    if args.only == "streaming":
+        out = streaming_frames(model, 0, 1, stream, RankGroup(1), total=max(args.batch, 256 * args.steps),
+                               batch=args.batch)
+    else:
+        ring = max(args.batch, 8)
+        frames = torch.empty((ring, 3, SIZE, SIZE), dtype=torch.float32, device="cuda")
+        _lib.check(_lib.lib().illumina_generate_frames(0 if args.only == "relight" else 1, 0, ring, SIZE,
+                                                       frames.data_ptr(), None))
+        if args.only == "relight":
+            out = depth_relight_frame(model, frames, ring, stream, ev0, ev1, reps=args.steps)
+        else:
+            disp = torch.empty((ring, SIZE, SIZE), dtype=torch.float32, device="cuda")
+            out = batch_sweep(model, frames, disp, stream, ev0, ev1, batches=(args.batch,))
+    model.destroy()
+    print(json.dumps({args.only: out}), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     rank, local_rank, world = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.only:
+        return run_only(args, local_rank) if rank == 0 else 0
     return run_ours(args, rank, local_rank, world)
 
 

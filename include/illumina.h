@@ -163,6 +163,15 @@ illumina_status illumina_model_set_temporal(illumina_model *model, float base_al
 illumina_status illumina_forward(illumina_model *model, const float *frames, int n, int frame_layout,
                                  float *disparity, float *depth_low, void *stream);
 
+/* forwardReference from a given network input (scripts/ref-forward.ts:296-300,
+ * an "input" bundle; src/model/reference.ts:360-451): `input` holds n x S x S x 4
+ * float32 channels-last preprocess outputs (host or device). Runs the stem as
+ * its own launch and the rest of the hot path; the bilateral guide is the
+ * input's channel 3 (the unnormalised luminance). fp32 models only.
+ * Synchronous; the intermediates are readable with debugTensor afterwards. */
+illumina_status illumina_forward_input(illumina_model *model, const float *input, int n, float *disparity,
+                                       float *depth_low);
+
 /* DepthModel.record for one streaming frame (runner.ts:440-449): like
  * illumina_forward with n = 1, but the bilateral upsample blends with the
  * temporal history held in the model's depth ping-pong and writes the depth
@@ -198,7 +207,10 @@ illumina_status illumina_model_debug_tensor(illumina_model *model, const char *n
 
 /* DepthModel.debugTensor (runner.ts:466-476) for frame `frame` (0 <= frame <
  * max_batch) of the last batched forward; illumina_model_debug_tensor is this
- * call with frame 0. INVALID_ARG for a frame outside the model's batch. */
+ * call with frame 0. INVALID_ARG for a frame outside the model's batch. The
+ * name "scene_color" reads the preprocess's second output (S x S x 4 linear
+ * colour, alpha 1; ref-forward.ts:286-292), which a keep-intermediates model
+ * keeps. */
 illumina_status illumina_model_debug_tensor_frame(illumina_model *model, const char *name, int frame, float *out,
                                                   size_t cap, int *h, int *w, int *c, int *live_at_end);
 
