@@ -12,10 +12,23 @@
 // fused as the epilogue, writing 8-bit RGBA directly: the HDR target is
 // optional.
 //
-// The depth map (448x448 float32 = 0.8 MB) stays resident in L2/L1 for the
-// ~90 dependent fetches per pixel; every fetch goes through the read-only
-// path. Step counts are runtime parameters so the reference constants and
-// longer marches share one kernel.
+// Depth neighbourhoods: each 16 x 8 block first stages the depth texels its
+// pixels can reach through the normal stencil (+-2) and the AO horizon
+// marches (+- the AO radius, up to kTileR) in a shared-memory tile, with the
+// reference's clamp-to-edge already applied, so those fetches are one shared
+// load with no clamping; the contact-shadow marches (screen projections of
+// view-space points) read the tile when they land in it and the read-only
+// cache otherwise.
+//
+// Arithmetic follows the accuracy WGSL specifies for the shader's built-ins
+// (division 2.5 ulp, inverseSqrt 2 ulp, sqrt as 1/inverseSqrt, exp 3 + 2|x|
+// ulp, pow via exp2(y log2 x), sin/cos 2^-11 absolute on [-pi, pi]): divisions
+// by the hardware reciprocal-based division, square roots and normalisations
+// by sqrt.approx / rsqrt.approx, exp / pow / sincos by the hardware
+// approximations. Loop invariants (reciprocals of the step counts, of the
+// projection scales and of the render size) are hoisted out of the marches.
+// Step counts are runtime parameters so the reference constants and longer
+// marches share one kernel.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -27,6 +40,23 @@ namespace gpu {
 
 namespace {
 
+constexpr int kShadeBX = 16, kShadeBY = 8;
+constexpr int kTileR = 24;       // tile halo bound: larger AO radii read beyond it from the cache
+constexpr int kTileMax = 3072;   // floats of the shared tile (12 KB)
+
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdividef(a, b); }
+__device__ __forceinline__ float frcp(float a) { return __fdividef(1.0f, a); }
+__device__ __forceinline__ float sqrt_a(float x) {
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rsqrt_a(float x) {
+  float r;
+  asm("rsqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 struct v3 {
   float x, y, z;
 };
@@ -35,10 +65,9 @@ __device__ __forceinline__ v3 operator+(v3 a, v3 b) { return mk(a.x + b.x, a.y +
 __device__ __forceinline__ v3 operator-(v3 a, v3 b) { return mk(a.x - b.x, a.y - b.y, a.z - b.z); }
 __device__ __forceinline__ v3 operator*(float s, v3 a) { return mk(s * a.x, s * a.y, s * a.z); }
 __device__ __forceinline__ v3 mulv(v3 a, v3 b) { return mk(a.x * b.x, a.y * b.y, a.z * b.z); }
-__device__ __forceinline__ v3 divs(v3 a, float s) { return mk(a.x / s, a.y / s, a.z / s); }
 __device__ __forceinline__ float dot3(v3 a, v3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
-__device__ __forceinline__ float len3(v3 a) { return sqrtf(dot3(a, a)); }
-__device__ __forceinline__ v3 norm3(v3 a) { return divs(a, len3(a)); }
+__device__ __forceinline__ float len3(v3 a) { return sqrt_a(dot3(a, a)); }
+__device__ __forceinline__ v3 norm3(v3 a) { return rsqrt_a(dot3(a, a)) * a; }
 __device__ __forceinline__ v3 cross3(v3 a, v3 b) {
   return mk(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);
 }
@@ -49,7 +78,7 @@ __device__ __forceinline__ v3 mixv(v3 a, v3 b, float t) {
 }
 __device__ __forceinline__ float fractf(float x) { return x - floorf(x); }
 __device__ __forceinline__ float smoothstepf(float e0, float e1, float x) {
-  float t = clampf((x - e0) / (e1 - e0), 0.0f, 1.0f);
+  float t = clampf(fdiv(x - e0, e1 - e0), 0.0f, 1.0f);
   return t * t * (3.0f - 2.0f * t);
 }
 __device__ __forceinline__ float pow4(float x) {
@@ -59,29 +88,33 @@ __device__ __forceinline__ float pow4(float x) {
 
 struct Ctx {
   const float *depth;
-  int dw, dh, dch;
+  int dw, dch;
   int maxX, maxY;
-  float szw, szh;  // size.z, size.w
-  float tanh_, aspect;
+  float szw, szh;          // size.z, size.w
+  float inv_szw, inv_szh;
+  float tanh_, atanh_;     // tan(fov/2), aspect * tan(fov/2)
   float inv_near_minus_far, inv_far;
+  // the block's shared tile: texels [tx0, tx0 + tw) x [ty0, ty0 + th), clamped
+  const float *tile;
+  int tx0, ty0, tw, th;
 };
 
 __device__ __forceinline__ float linear_depth(const Ctx &c, float d) {
-  float invZ = d * c.inv_near_minus_far + c.inv_far;
-  return 1.0f / fmaxf(invZ, 1e-6f);
+  return frcp(fmaxf(d * c.inv_near_minus_far + c.inv_far, 1e-6f));
 }
 __device__ __forceinline__ float fetch(const Ctx &c, int x, int y) {
+  const unsigned lx = (unsigned)(x - c.tx0), ly = (unsigned)(y - c.ty0);
+  if (lx < (unsigned)c.tw && ly < (unsigned)c.th) return c.tile[ly * c.tw + lx];
   x = min(max(x, 0), c.maxX);
   y = min(max(y, 0), c.maxY);
   return __ldg(c.depth + ((long)y * c.dw + x) * c.dch);
 }
 __device__ __forceinline__ v3 view_position(const Ctx &c, float u, float v, float z) {
   float ndcX = u * 2.0f - 1.0f, ndcY = 1.0f - v * 2.0f;
-  return mk(ndcX * c.aspect * c.tanh_ * z, ndcY * c.tanh_ * z, -z);
+  return mk(ndcX * c.atanh_ * z, ndcY * c.tanh_ * z, -z);
 }
-__device__ __forceinline__ v3 view_position_at(const Ctx &c, int x, int y) {
-  float u = ((float)x + 0.5f) / c.szw, v = ((float)y + 0.5f) / c.szh;
-  return view_position(c, u, v, linear_depth(c, fetch(c, x, y)));
+__device__ __forceinline__ v3 view_position_px(const Ctx &c, int x, int y, float d) {
+  return view_position(c, ((float)x + 0.5f) * c.inv_szw, ((float)y + 0.5f) * c.inv_szh, linear_depth(c, d));
 }
 
 __device__ v3 reconstruct_normal(const Ctx &c, int x, int y) {
@@ -92,41 +125,32 @@ __device__ v3 reconstruct_normal(const Ctx &c, int x, int y) {
   float b1 = fetch(c, x, y + 1), b2 = fetch(c, x, y + 2);
   float errL = fabsf(2.0f * l1 - l2 - cc), errR = fabsf(2.0f * r1 - r2 - cc);
   float errU = fabsf(2.0f * u1 - u2 - cc), errB = fabsf(2.0f * b1 - b2 - cc);
-  // The five positions reuse the fetched disparities.
-  auto pos = [&](int px, int py, float d) {
-    float u = ((float)px + 0.5f) / c.szw, v = ((float)py + 0.5f) / c.szh;
-    return view_position(c, u, v, linear_depth(c, d));
-  };
-  // fetch() clamps coordinates; pos() must use the clamped coordinate's
-  // disparity but the unclamped pixel centre, as viewPositionAt does.
-  v3 pc = pos(x, y, cc);
-  v3 dxL = pc - pos(x - 1, y, l1);
-  v3 dxR = pos(x + 1, y, r1) - pc;
-  v3 dyU = pc - pos(x, y - 1, u1);
-  v3 dyD = pos(x, y + 1, b1) - pc;
-  v3 dx = errL < errR ? dxL : dxR;
-  v3 dy = errU < errB ? dyU : dyD;
+  // the positions use the clamped texel's disparity at the unclamped pixel
+  // centre, as viewPositionAt does; only the chosen side of each axis is built
+  v3 pc = view_position_px(c, x, y, cc);
+  v3 dx = errL < errR ? pc - view_position_px(c, x - 1, y, l1) : view_position_px(c, x + 1, y, r1) - pc;
+  v3 dy = errU < errB ? pc - view_position_px(c, x, y - 1, u1) : view_position_px(c, x, y + 1, b1) - pc;
   v3 n = cross3(dy, dx);
-  float l = len3(n);
-  return l > 1e-12f ? divs(n, l) : mk(0, 0, 1);
+  float l2n = dot3(n, n);
+  return l2n > 1e-24f ? rsqrt_a(l2n) * n : mk(0, 0, 1);
 }
 
-__device__ float contact_shadow(const Ctx &c, v3 origin, v3 to_light, float max_len, float jitter, int steps) {
-  v3 step = (max_len / (float)steps) * to_light;
+__device__ float contact_shadow(const Ctx &c, v3 origin, v3 to_light, float max_len, float jitter, int steps,
+                                float inv_steps) {
+  v3 step = (max_len * inv_steps) * to_light;
   float occlusion = 0.0f;
   v3 p = origin + jitter * step;
+  const float kx = frcp(c.atanh_), ky = frcp(c.tanh_);
   for (int i = 0; i < steps; i++) {
     p = p + step;
-    float z = fmaxf(-p.z, 1e-4f);
-    float ndcX = p.x / (c.aspect * c.tanh_ * z);
-    float ndcY = p.y / (c.tanh_ * z);
-    float u = ndcX * 0.5f + 0.5f, v = 0.5f - ndcY * 0.5f;
+    float inv_z = frcp(fmaxf(-p.z, 1e-4f));
+    float u = (p.x * kx * inv_z) * 0.5f + 0.5f, v = 0.5f - (p.y * ky * inv_z) * 0.5f;
     if (u > 0.0f && u < 1.0f && v > 0.0f && v < 1.0f) {
       int cx = (int)(u * c.szw), cy = (int)(v * c.szh);
       float sceneZ = linear_depth(c, fetch(c, cx, cy));
       float delta = -p.z - sceneZ;
       float thickness = fmaxf(0.35f, sceneZ * 0.08f);
-      if (delta > 0.012f && delta < thickness) occlusion = fmaxf(occlusion, 1.0f - (float)i / (float)steps);
+      if (delta > 0.012f && delta < thickness) occlusion = fmaxf(occlusion, 1.0f - (float)i * inv_steps);
     }
   }
   return 1.0f - clampf(occlusion, 0.0f, 1.0f);
@@ -135,49 +159,52 @@ __device__ float contact_shadow(const Ctx &c, v3 origin, v3 to_light, float max_
 __device__ float horizon_occlusion(const Ctx &c, int x, int y, v3 position, v3 normal, float radius_px,
                                    float jitter, int dirs, int steps) {
   float total = 0.0f;
+  const float inv_dirs = frcp((float)dirs), inv_steps = frcp((float)steps);
   for (int i = 0; i < dirs; i++) {
-    float angle = (((float)i + jitter) / (float)dirs) * 6.2831853f;
+    float angle = (((float)i + jitter) * inv_dirs) * 6.2831853f;
+    if (angle > 3.14159265f) angle -= 6.2831853f;  // sin/cos of the same angle, on [-pi, pi]
     float s_, c_;
-    sincosf(angle, &s_, &c_);
+    __sincosf(angle, &s_, &c_);
     float horizon = -1.0f;
     for (int s = 0; s < steps; s++) {
-      float dist = radius_px * (((float)s + 1.0f) / (float)steps);
+      float dist = radius_px * (((float)s + 1.0f) * inv_steps);
       int sx = x + (int)(c_ * dist), sy = y + (int)(s_ * dist);
-      v3 diff = view_position_at(c, sx, sy) - position;
-      float l = len3(diff);
-      if (l > 1e-5f) {
-        float cosH = dot3(normal, divs(diff, l));
-        float falloff = clampf(1.0f - (l * l) / 9.0f, 0.0f, 1.0f);
+      v3 diff = view_position_px(c, sx, sy, fetch(c, sx, sy)) - position;
+      float l2 = dot3(diff, diff);
+      float inv_l = rsqrt_a(l2);
+      if (l2 * inv_l > 1e-5f) {
+        float cosH = dot3(normal, diff) * inv_l;
+        float falloff = clampf(1.0f - l2 * (1.0f / 9.0f), 0.0f, 1.0f);
         horizon = fmaxf(horizon, cosH * falloff);
       }
     }
     total += fmaxf(horizon, 0.0f);
   }
-  return clampf(1.0f - total / (float)dirs, 0.0f, 1.0f);
+  return clampf(1.0f - total * inv_dirs, 0.0f, 1.0f);
 }
 
 __device__ __forceinline__ float ggx_d(float nDotH, float roughness) {
   float r = fmaxf(roughness, 1e-3f);
   float a = r * r;
   float a2 = a * a;
-  float denom = fmaf(nDotH * nDotH, a2 - 1.0f, 1.0f);  // one rounding, as the oracle
-  return a2 / (3.14159265f * denom * denom + 1e-20f);
+  float denom = fmaf(nDotH * nDotH, a2 - 1.0f, 1.0f);
+  return fdiv(a2, 3.14159265f * denom * denom + 1e-20f);
 }
 __device__ __forceinline__ float smith_g(float nDotV, float nDotL, float roughness) {
-  float k = (roughness + 1.0f) * (roughness + 1.0f) / 8.0f;
-  return (nDotV / (nDotV * (1.0f - k) + k)) * (nDotL / (nDotL * (1.0f - k) + k));
+  float k = (roughness + 1.0f) * (roughness + 1.0f) * 0.125f;
+  return fdiv(nDotV, nDotV * (1.0f - k) + k) * fdiv(nDotL, nDotL * (1.0f - k) + k);
 }
 __device__ __forceinline__ float srgb_to_linear(float v) {
-  return v <= 0.04045f ? v / 12.92f : powf((v + 0.055f) / 1.055f, 2.4f);
+  return v <= 0.04045f ? v * (1.0f / 12.92f) : __powf((v + 0.055f) * (1.0f / 1.055f), 2.4f);
 }
 __device__ __forceinline__ float linear_to_srgb(float v) {
-  return v <= 0.0031308f ? 12.92f * v : 1.055f * powf(v, 1.0f / 2.4f) - 0.055f;
+  return v <= 0.0031308f ? 12.92f * v : 1.055f * __powf(v, 1.0f / 2.4f) - 0.055f;
 }
 __device__ __forceinline__ float aces1(float x) {
-  return clampf((x * (2.51f * x + 0.03f)) / (x * (2.43f * x + 0.59f) + 0.14f), 0.0f, 1.0f);
+  return clampf(fdiv(x * (2.51f * x + 0.03f), x * (2.43f * x + 0.59f) + 0.14f), 0.0f, 1.0f);
 }
 __device__ __forceinline__ float reinhard1(float x) {
-  return clampf((x * (1.0f + x / 16.0f)) / (1.0f + x), 0.0f, 1.0f);
+  return clampf(fdiv(x * (1.0f + x * (1.0f / 16.0f)), 1.0f + x), 0.0f, 1.0f);
 }
 __device__ __forceinline__ uint32_t unorm8(float v) {
   if (!(v > 0.0f)) return 0u;
@@ -191,23 +218,48 @@ struct LightSet {
 
 }  // namespace
 
-__global__ void __launch_bounds__(128) k_shade(const float *__restrict__ depth, int dw, int dh, int dch,
-                                               const float *__restrict__ albedo, int aw, int ah, LightSet L,
-                                               ShadeParams P, ShadeSteps st, int out_w, int out_h, float *hdr,
-                                               uint8_t *rgba8) {
-  int px = blockIdx.x * blockDim.x + threadIdx.x;
-  int py = blockIdx.y * blockDim.y + threadIdx.y;
-  if (px >= out_w || py >= out_h) return;
+__global__ void __launch_bounds__(kShadeBX * kShadeBY) k_shade(const float *__restrict__ depth, int dw, int dh,
+                                                               int dch, const float *__restrict__ albedo, int aw,
+                                                               int ah, LightSet L, ShadeParams P, ShadeSteps st,
+                                                               int out_w, int out_h, float *hdr, uint8_t *rgba8) {
+  __shared__ float tile[kTileMax];
+  const int px = blockIdx.x * kShadeBX + threadIdx.x;
+  const int py = blockIdx.y * kShadeBY + threadIdx.y;
   Ctx c;
-  c.depth = depth, c.dw = dw, c.dh = dh, c.dch = dch;
+  c.depth = depth, c.dw = dw, c.dch = dch;
   c.maxX = (int)P.size[2] - 1, c.maxY = (int)P.size[3] - 1;
   c.szw = P.size[2], c.szh = P.size[3];
-  c.tanh_ = P.camera[0], c.aspect = P.camera[1];
+  c.inv_szw = 1.0f / P.size[2], c.inv_szh = 1.0f / P.size[3];
+  c.tanh_ = P.camera[0], c.atanh_ = P.camera[1] * P.camera[0];
   float near = fmaxf(P.camera[2], 1e-3f), far = fmaxf(P.camera[3], near + 1e-3f);
   c.inv_near_minus_far = 1.0f / near - 1.0f / far;
   c.inv_far = 1.0f / far;
+  const float inv_w = 1.0f / P.size[0], inv_h = 1.0f / P.size[1];
 
-  float u = ((float)px + 0.5f) / P.size[0], v = ((float)py + 0.5f) / P.size[1];
+  // ---- stage the block's depth neighbourhood (clamp-to-edge applied) ----
+  {
+    const int bx0 = blockIdx.x * kShadeBX, by0 = blockIdx.y * kShadeBY;
+    const int bx1 = min(bx0 + kShadeBX, out_w) - 1, by1 = min(by0 + kShadeBY, out_h) - 1;
+    const int dx0 = (int)(((float)bx0 + 0.5f) * inv_w * P.size[2]), dx1 = (int)(((float)bx1 + 0.5f) * inv_w * P.size[2]);
+    const int dy0 = (int)(((float)by0 + 0.5f) * inv_h * P.size[3]), dy1 = (int)(((float)by1 + 0.5f) * inv_h * P.size[3]);
+    const float ao_r = P.toggles[0] > 0.001f ? P.debug[3] : 0.0f;
+    const int R = max(2, min(kTileR, (int)fminf(fmaxf(ao_r, 0.0f), (float)kTileR)));
+    c.tx0 = dx0 - R, c.ty0 = dy0 - R;
+    c.tw = dx1 - dx0 + 1 + 2 * R, c.th = dy1 - dy0 + 1 + 2 * R;
+    if (c.tw * c.th > kTileMax) c.tw = c.th = 0;  // every fetch goes through the cache
+    const int n = c.tw * c.th;
+    const int tid = threadIdx.y * kShadeBX + threadIdx.x;
+    for (int i = tid; i < n; i += kShadeBX * kShadeBY) {
+      const int ly = i / c.tw, lx = i - ly * c.tw;
+      const int x = min(max(c.tx0 + lx, 0), c.maxX), y = min(max(c.ty0 + ly, 0), c.maxY);
+      tile[i] = __ldg(depth + ((long)y * dw + x) * dch);
+    }
+    c.tile = tile;
+    __syncthreads();
+  }
+  if (px >= out_w || py >= out_h) return;
+
+  float u = ((float)px + 0.5f) * inv_w, v = ((float)py + 0.5f) * inv_h;
   int dcx = (int)(u * P.size[2]), dcy = (int)(v * P.size[3]);
   float disparity = fetch(c, dcx, dcy);
   float z = linear_depth(c, disparity);
@@ -248,7 +300,8 @@ __global__ void __launch_bounds__(128) k_shade(const float *__restrict__ depth, 
   v3 radiance = mulv((P.ambient[3] * ao) * albedo_c, mk(P.ambient[0], P.ambient[1], P.ambient[2]));
   v3 scattering = mk(0, 0, 0);
   float ray_len = len3(position);
-  v3 ray_dir = divs(position, fmaxf(ray_len, 1e-5f));
+  v3 ray_dir = frcp(fmaxf(ray_len, 1e-5f)) * position;
+  const float inv_contact = frcp((float)st.contact), inv_vol = frcp((float)st.volumetric);
 
   for (int li = 0; li < 8; li++) {
     const ShadeLight &Lt = L.l[li];
@@ -259,20 +312,21 @@ __global__ void __launch_bounds__(128) k_shade(const float *__restrict__ depth, 
     v3 lpos = mk(Lt.position[0], Lt.position[1], Lt.position[2]);
     v3 to_light = mk(0, 0, 1);
     float atten = 1.0f, distance = 1e6f;
+    const float inv_range = frcp(fmaxf(Lt.params[2], 1e-3f));
     if (kind > 1.5f) {
       to_light = norm3(-1.0f * lpos);
     } else {
       v3 delta = lpos - position;
       distance = fmaxf(len3(delta), 1e-4f);
-      to_light = divs(delta, distance);
-      float range = fmaxf(Lt.params[2], 1e-3f);
-      float win = clampf(1.0f - pow4(distance / range), 0.0f, 1.0f);
-      atten = (win * win) / (distance * distance + 1e-4f);
+      to_light = frcp(distance) * delta;
+      float win = clampf(1.0f - pow4(distance * inv_range), 0.0f, 1.0f);
+      atten = fdiv(win * win, distance * distance + 1e-4f);
     }
     v3 axis = mk(Lt.direction[0], Lt.direction[1], Lt.direction[2]);
+    const float cone_hi = fmaxf(Lt.params[1], Lt.direction[3] + 1e-3f);
     if (kind > 0.5f && kind < 1.5f) {
-      float cosA = dot3(-1.0f * to_light, axis);
-      atten *= smoothstepf(Lt.direction[3], fmaxf(Lt.params[1], Lt.direction[3] + 1e-3f), cosA);
+      float cosA = -dot3(to_light, axis);
+      atten *= smoothstepf(Lt.direction[3], cone_hi, cosA);
     }
     float nDotL = dot3(normal, to_light);
     if (nDotL > 0.0f && atten > 0.0f) {
@@ -280,7 +334,7 @@ __global__ void __launch_bounds__(128) k_shade(const float *__restrict__ depth, 
       float amount = Lt.params[3] * P.toggles[1];
       if (amount > 0.0f) {
         float march = fminf(P.debug[2], distance);
-        shadow = mixf(1.0f, contact_shadow(c, position, to_light, march, jitter, st.contact), amount);
+        shadow = mixf(1.0f, contact_shadow(c, position, to_light, march, jitter, st.contact, inv_contact), amount);
       }
       v3 half = norm3(to_light + view_dir);
       float nDotH = fmaxf(dot3(normal, half), 0.0f);
@@ -289,24 +343,29 @@ __global__ void __launch_bounds__(128) k_shade(const float *__restrict__ depth, 
       radiance = radiance + energy * mulv(lcol, albedo_c + mk(spec, spec, spec));
     }
     if (P.toggles[2] > 0.0f && kind < 1.5f) {
-      float step_len = ray_len / (float)st.volumetric;
-      float range = fmaxf(Lt.params[2], 1e-3f);
+      const float step_len = ray_len * inv_vol;
+      const float k = intensity * step_len * P.misc[2];
+      float acc = 0.0f;
+      const float inv_range2 = inv_range * inv_range;
       for (int s = 0; s < st.volumetric; s++) {
-        float t = (((float)s + jitter) / (float)st.volumetric) * ray_len;
+        float t = ((float)s + jitter) * step_len;
         v3 toL = lpos - t * ray_dir;
-        float dist = fmaxf(len3(toL), 1e-3f);
-        float win = clampf(1.0f - pow4(dist / range), 0.0f, 1.0f);
-        float att = (win * win) / (dist * dist + 1e-4f);
+        // dist = max(|toL|, 1e-3) enters only squared: no square root
+        float dd = fmaxf(dot3(toL, toL), 1e-6f);
+        float q = dd * inv_range2;  // (dist / range)^2
+        float win = clampf(1.0f - q * q, 0.0f, 1.0f);
+        float att = fdiv(win * win, dd + 1e-4f);
         if (kind > 0.5f) {
-          float cosA = dot3(-1.0f * divs(toL, dist), axis);
-          att *= smoothstepf(Lt.direction[3], fmaxf(Lt.params[1], Lt.direction[3] + 1e-3f), cosA);
+          float cosA = -dot3(toL, axis) * rsqrt_a(dd);
+          att *= smoothstepf(Lt.direction[3], cone_hi, cosA);
         }
-        scattering = scattering + (att * intensity * step_len * P.misc[2]) * lcol;
+        acc += att;
       }
+      scattering = scattering + (acc * k) * lcol;
     }
   }
   radiance = radiance + P.toggles[2] * scattering;
-  float fog_amount = 1.0f - expf(-z * P.misc[2]);
+  float fog_amount = 1.0f - __expf(-z * P.misc[2]);
   radiance = mixv(radiance, mk(P.fog[0], P.fog[1], P.fog[2]), clampf(fog_amount, 0.0f, 1.0f));
   radiance = P.toggles[3] * radiance;
   float mode = P.debug[0];
@@ -340,8 +399,8 @@ cudaError_t shade(const float *depth, int dw, int dh, int dch, const float *albe
   if (out_w <= 0 || out_h <= 0) return cudaSuccess;
   LightSet L;
   for (int i = 0; i < 8; i++) L.l[i] = lights[i];
-  dim3 block(16, 8);
-  dim3 grid((out_w + 15) / 16, (out_h + 7) / 8);
+  dim3 block(kShadeBX, kShadeBY);
+  dim3 grid((out_w + kShadeBX - 1) / kShadeBX, (out_h + kShadeBY - 1) / kShadeBY);
   k_shade<<<grid, block, 0, st>>>(depth, dw, dh, dch, albedo, aw, ah, L, P, steps, out_w, out_h, hdr, rgba8);
   return cudaGetLastError();
 }
