@@ -66,13 +66,11 @@ struct GemmOp {
   const float *dw_w = nullptr;   // packed [ks*ks][K]
   const float *dw_b = nullptr;   // [K]
   const void *coarse = nullptr;  // lateral: (n, H/2, W/2, N)
-  // Optional split-K workspace of the tensor-core dw->pw kernel: fp32 partial
-  // tiles and one zero-initialised arrival counter per work item (the kernel
-  // leaves them zero again). Without it the kernel does not split K.
+  // Optional split-K workspace of the tensor-core kernels: fp32 partial tiles
+  // of the K splits, summed by a reduction launch that follows the op's
+  // kernel. Without it the kernels do not split K.
   float *ws = nullptr;
   size_t ws_bytes = 0;
-  int *ws_cnt = nullptr;
-  int ws_cnt_n = 0;
   // Optional depth head on the op's output (dw->pw on the tensor engine):
   // head_dst[m] = sigmoid(head_b + sum_n dst[m][n] * head_w[n]), folded into
   // the epilogue when the launch allows it, else a separate head launch.

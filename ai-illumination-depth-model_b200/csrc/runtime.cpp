@@ -50,13 +50,11 @@ void set_last_error(const std::string &msg) { g_last_error = msg; }
 
 namespace {
 
-// Split-K workspace of the tensor-core dw->pw kernel: a model holds 16 MiB of
-// fp32 partial tiles and 8192 arrival counters (the planner splits K only
-// when a launch's partials fit); a per-kernel entry point call takes 8 MiB.
+// Split-K workspace of the tensor-core kernels: a model holds 16 MiB of fp32
+// partial tiles (the planners split K only when a launch's partials fit); a
+// per-kernel entry point call takes 8 MiB.
 constexpr size_t kSplitKBytes = 16u << 20;
-constexpr int kSplitKItems = 8192;
 constexpr size_t kSplitKOpBytes = 8u << 20;
-constexpr int kSplitKOpItems = 4096;
 // Largest batch whose forward uses programmatic dependent launch.
 constexpr int kPdlMaxBatch = 16;
 
@@ -152,7 +150,6 @@ struct illumina_model {
   int *d_err = nullptr;              // device address of h_err
   long long wait_cycles = 0;         // tensor kernels' pipeline wait limit (0: the kernels' default)
   float *d_splitk = nullptr;         // split-K partial tiles of the tensor dw->pw kernel
-  int *d_splitk_cnt = nullptr;       // its per-item arrival counters (zero between launches)
   int stem_fused_op = -1;            // conv op folded into the preprocess launch, or -1
   int head_fused_op = -1;            // head op folded into the preceding dw->pw launch, or -1
   bool stem_writes_input = true;     // the folded launch still writes the network input
@@ -188,7 +185,6 @@ illumina_model::~illumina_model() {
   cudaFree(d_wimg);
   if (h_err) cudaFreeHost((void *)h_err);
   cudaFree(d_splitk);
-  cudaFree(d_splitk_cnt);
   if (ev_join) cudaEventDestroy(ev_join);
   if (ev_done) cudaEventDestroy(ev_done);
   for (int i = 0; i < kMaxChunks; i++) {
@@ -377,7 +373,6 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
             g.mid_act = op.mid_act;
             g.dw_w = w.dw_w, g.dw_b = w.dw_b;
             g.ws = m.d_splitk, g.ws_bytes = m.d_splitk ? kSplitKBytes : 0;
-            g.ws_cnt = m.d_splitk_cnt, g.ws_cnt_n = m.d_splitk_cnt ? kSplitKItems : 0;
             if ((int)i + 1 == m.head_fused_op) {
               // the head that reads this op's output runs in its epilogue
               const OpWeights &hw = m.opw[i + 1];
@@ -517,17 +512,12 @@ int host_chunks(int n, int *sizes) {
 
 // Reports a bounded device wait that gave up (the kernels set the model's
 // error word and left the rest of their work undone, so the outputs of the
-// forward that ran them are undefined): clears the word, returns the split-K
-// arrival counters (which a unit that gave up may have left non-zero) to zero
-// and throws TIMEOUT. `when` says which call's kernels the word covers.
+// forward that ran them are undefined): clears the word and throws TIMEOUT.
+// `when` says which call's kernels the word covers.
 void check_timeout(illumina_model &m, const char *when) {
   if (!m.h_err || *m.h_err == 0) return;
   cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
   *m.h_err = 0;
-  if (m.d_splitk_cnt) {
-    cuda_check(cudaMemsetAsync(m.d_splitk_cnt, 0, kSplitKItems * sizeof(int), m.stream), "clear split-K counters");
-    cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
-  }
   throw Error(ILLUMINA_TIMEOUT, std::string("a tensor-core kernel gave up a bounded wait (") + when +
                                     "); the outputs of that forward are undefined, the model is usable again");
 }
@@ -769,9 +759,7 @@ void build_model(illumina_model &m, const illumina_model_options &o) {
   }
   if (o.gemm_engine == ILLUMINA_ENGINE_TENSOR) {
     cuda_check(cudaMalloc(&m.d_splitk, kSplitKBytes), "cudaMalloc split-K workspace");
-    cuda_check(cudaMalloc(&m.d_splitk_cnt, kSplitKItems * sizeof(int)), "cudaMalloc split-K counters");
-    cuda_check(cudaMemsetAsync(m.d_splitk_cnt, 0, kSplitKItems * sizeof(int), m.stream), "clear split-K counters");
-    m.device_bytes += kSplitKBytes + kSplitKItems * sizeof(int);
+    m.device_bytes += kSplitKBytes;
   }
   m.tcw.resize(m.arch.ops.size());
   m.tc_off.assign(m.arch.ops.size(), 0);
@@ -864,10 +852,9 @@ void op_gemm(const gpu::GemmOp &g, cudaStream_t st, const char *what) {
     return;
   }
   cuda_check(gpu::tc_pack_dw(gpu::F32, g.dw_w, g.dw_b, plan, (uint8_t *)img.p, st), "pack depthwise blocks");
-  Scratch ws(kSplitKOpBytes, st), cnt(kSplitKOpItems * sizeof(int), st);
-  cuda_check(cudaMemsetAsync(cnt.p, 0, kSplitKOpItems * sizeof(int), st), "clear split-K counters");
+  Scratch ws(kSplitKOpBytes, st);
   gpu::GemmOp gs = g;
-  gs.ws = (float *)ws.p, gs.ws_bytes = kSplitKOpBytes, gs.ws_cnt = (int *)cnt.p, gs.ws_cnt_n = kSplitKOpItems;
+  gs.ws = (float *)ws.p, gs.ws_bytes = kSplitKOpBytes;
   cuda_check(gpu::tc_op(gpu::F32, gs, plan, (const uint8_t *)img.p, nullptr, st), what);
 }
 

@@ -74,6 +74,11 @@ template <uint32_t N>
 __device__ __forceinline__ void reg_dealloc() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
+// Brings a kernel-parameter TMA descriptor into the descriptor cache ahead of
+// its first copy.
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -458,11 +463,13 @@ struct PatchMap {
 };
 
 // Split-K: sums the ksplit partial tiles of one item ([ksplit][128][ld] at
-// `part`; split order fixed, so the result does not depend on which CTA
-// finished last), then bias, residual, activation and store. The nw calling
-// warps (warp index wi) share (8-row group, 16-column block) units; groups
-// beyond the patch's th*tw rows are skipped. Four splits' loads are in flight
-// at once; partials are read past L1 (written by other SMs).
+// `part`; split order fixed, so the result does not depend on the order in
+// which the splits were computed), then bias, residual, activation and store.
+// a.bias holds the tile's bias (column c of the tile at a.bias[c], 16-byte
+// aligned). The nw calling warps (warp index wi) share (8-row group, 16-column
+// block) units; groups beyond the patch's th*tw rows are skipped. Four
+// splits' loads are in flight at once; partials are read past L1 (written by
+// other SMs).
 template <typename T, int ACT>
 __device__ __forceinline__ void reduce_units(const EpiArgs &a, const float *part, int ksplit, size_t split_stride,
                                              int ld, int ncols, int n_base, const PatchMap &pm, int wi, int nw) {
@@ -490,7 +497,7 @@ __device__ __forceinline__ void reduce_units(const EpiArgs &a, const float *part
       for (int k = 0; k < 4; k++)
         if (j + k < ksplit) o.x += q[k].x, o.y += q[k].y, o.z += q[k].z, o.w += q[k].w;
     }
-    const float4 bias = *reinterpret_cast<const float4 *>(a.bias + n);
+    const float4 bias = *reinterpret_cast<const float4 *>(a.bias + c);
     o.x += bias.x, o.y += bias.y, o.z += bias.z, o.w += bias.w;
     if (res) {
       const float4 q = ld4(res + m * a.N + n);

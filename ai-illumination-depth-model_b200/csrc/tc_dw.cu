@@ -109,9 +109,10 @@ struct DwTiling {
 // serialised otherwise; `ng` groups interleave; the MMAs, the halo bandwidth
 // and the shared-memory wavefronts (depthwise loads and stores, UMMA operand
 // reads, TMA writes) bound the step from below. A split item adds the partial
-// tile store and, on the CTA that finishes it, the reduction.
+// tile store, and the launch a reduction kernel whose (8-row, 16-column)
+// units spread over every SM.
 DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const TcWeights &w, bool has_res,
-                     size_t ws_bytes, int cnt_n) {
+                     size_t ws_bytes) {
   const bool f32 = T == F32;
   const size_t bias_bytes = align_to((size_t)w.N * 4, 16);
   const int terms = f32 ? 2 : 1, slab_c = f32 ? 32 : 64, cgs = slab_c / 4;
@@ -162,21 +163,23 @@ DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const 
                 if (sg / ng < 2) group += mma;
                 const double per_slab = std::fmax(std::fmax(group / ng, mma), std::fmax(bw, smem_rd));
                 int last_ks = 0;
-                for (int want = 1; want <= std::min(w.slabs, 16); want++) {
+                for (int want = 1; want <= std::min(w.slabs, 32); want++) {
                   const int spk = (w.slabs + want - 1) / want;
                   const int ks = (w.slabs + spk - 1) / spk;
                   if (ks == last_ks) continue;
                   last_ks = ks;
-                  if (ks > 1 && (items * ks * kTileMBytes(w.n_tile) > (double)ws_bytes || items > cnt_n)) break;
+                  if (ks > 1 && items * ks * kTileMBytes(w.n_tile) > (double)ws_bytes) break;
                   const double nunits = items * ks;
                   const double waves = std::ceil(nunits / G);
-                  // split: partial store per unit, and on the finishing CTA a
-                  // reduction whose (8-row, 16-column) units are latency bound
-                  // (four splits' loads in flight per unit, four warps)
+                  // split: partial store per unit, then the reduction launch
+                  // (~4000 cycles to start behind this kernel) whose latency-bound
+                  // (8-row, 16-column) units (four splits' loads in flight per
+                  // unit) run one per warp, 32 warps per SM
                   const double red_units = std::ceil(th * tw / 8.0) * std::ceil(w.n_tile / 16.0);
                   const double per_unit = std::fmax(spk * per_slab, epi) + (ks > 1 ? 300.0 * w.n_tile / 16 : 0.0);
-                  const double red =
-                      ks > 1 ? 1500.0 + std::ceil(red_units / 4) * (std::ceil(ks / 4.0) * 700.0 + 150.0) : 0.0;
+                  const double red = ks > 1 ? 4000.0 + std::ceil(items * red_units / (G * 32.0)) *
+                                                           (std::ceil(ks / 4.0) * 700.0 + 150.0)
+                                            : 0.0;
                   const double cost = (waves * per_unit + red) * (b_res ? 0.99 : 1.0) * (1.0 - 0.001 * (sh + sg));
                   if (best.tw == 0 || cost < best.cost) {
                     best.tw = tw, best.th = th, best.P = P, best.iw = iw, best.ih = ih, best.ng = ng;
@@ -196,15 +199,15 @@ DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const 
 
 // plan_tiling is a few-thousand-candidate search; launches of one shape reuse it.
 DwTiling cached_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const TcWeights &w, bool has_res,
-                       size_t ws_bytes, int cnt_n) {
+                       size_t ws_bytes) {
   using Key = std::array<long, 12>;
   static std::mutex mu;
   static std::map<Key, DwTiling> cache;
-  const Key key{T, n_frames, OH, OW, KS, S, w.N, w.K, has_res ? 1 : 0, (long)ws_bytes, cnt_n, sm_count()};
+  const Key key{T, n_frames, OH, OW, KS, S, w.N, w.K, has_res ? 1 : 0, (long)ws_bytes, 0, sm_count()};
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  const DwTiling t = plan_tiling(T, n_frames, OH, OW, KS, S, w, has_res, ws_bytes, cnt_n);
+  const DwTiling t = plan_tiling(T, n_frames, OH, OW, KS, S, w, has_res, ws_bytes);
   cache.emplace(key, t);
   return t;
 }
@@ -238,7 +241,7 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
   const DwTiling tl = cached_tiling(T, op.n, op.OH, op.OW, op.ks, op.stride, plan, op.res != nullptr,
-                                    op.ws ? op.ws_bytes : 0, op.ws_cnt ? op.ws_cnt_n : 0);
+                                    op.ws ? op.ws_bytes : 0);
   if (tl.tw == 0) return cudaErrorInvalidValue;
 
   const size_t elt = T == F32 ? 4 : 2;
@@ -280,7 +283,7 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   const long total = items * tl.ksplit;
   if (total > 0x7fffffffL) return cudaErrorInvalidValue;
   p.items = (int)items, p.ksplit = tl.ksplit, p.spk = tl.spk, p.total = (int)total;
-  p.ws = op.ws, p.cnt = op.ws_cnt;
+  p.ws = op.ws;
   p.tw = tl.tw, p.th = tl.th, p.iw = tl.iw, p.mid_act = op.mid_act;
   {
     const int k_last = op.K - (plan.slabs - 1) * slab_c;  // channels in the last slab

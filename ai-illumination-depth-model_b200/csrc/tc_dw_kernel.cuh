@@ -79,7 +79,6 @@ struct Params {
   int *err;
   long long wait;  // cycles a pipeline wait may take before the role gives up
   float *ws;  // split-K partial tiles [item][split][128][n_tile] (ksplit > 1)
-  int *cnt;   // split-K arrival counters [item], zero between launches
   int tiles_x, tiles_y, n_tiles, slabs, items, ksplit, spk, total;  // total = items * ksplit units
   int tw, th, iw, mid_act;
   // last K slab: 32-byte K chunks holding channels (MMAs issued) and the
@@ -236,7 +235,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
   uint64_t *b_full = acc_empty + 2;
   uint64_t *drain = b_full + 1;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-  volatile uint32_t *last_flag = tmem_slot + 1;  // split-K: this CTA reduces the item
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tile = p.epi.n_tile;
@@ -259,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     fence_barrier_init();
   }
   if (tid == 0) pdl_trigger();
-  for (int i = tid; i < p.epi.N; i += kThreads) bias_smem[i] = p.epi.bias[i];
+  if (tid == 32) prefetch_tmap(&tmap), prefetch_tmap(&tmap_out);
   if (warp == 0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
   __syncthreads();
@@ -418,6 +416,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
     const int tw = p.tw, th = p.th, OH = p.epi.OH, OW = p.epi.OW;
     EpiArgs ea = p.epi;
     ea.bias = bias_smem;
+    // the bias is staged here by both teams, off the CTA's set-up path (only
+    // the epilogue reads it)
+    for (int i = tid - kEpiWarp0 * 32; i < p.epi.N; i += kEpiTeams * kEpiW * 32) bias_smem[i] = p.epi.bias[i];
+    bar_named(3, kEpiTeams * kEpiW * 32);
     pdl_wait();  // residual reads, split-K workspace and stores follow the previous kernel
     auto pix_of = [=](const Item &it) {
       return [=](int r) -> long {
@@ -486,10 +488,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
       }
       if (elected) bulk_wait_all();  // the output is written before the CTA leaves
     } else {
-      // split-K: write this split's partial tile, release the accumulator; the
-      // CTA that brings the item's last partial sums them and stores the item.
-      // The four epilogue warps agree on every outcome through named barrier 1,
-      // so none of them is left waiting at it.
+      // split-K: write this split's partial tile and release the accumulator;
+      // k_splitk_reduce, launched after this kernel, sums the item's partials
+      // in split order and stores the item. The four epilogue warps agree on
+      // every wait's outcome through named barrier 1.
       const size_t tile_elems = (size_t)kTileM * n_tile;
       for (int t = t_first; t < p.total && ok; t += t_step) {
         const Item it = decode<SPLIT>(p, t);
@@ -506,17 +508,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
         next_acc();
-        __threadfence();
-        bar_named(1, kEpiW * 32);
-        if (warp == kEpiWarp0 && lane == 0) *last_flag = atomicAdd(&p.cnt[it.id], 1) == p.ksplit - 1 ? 1u : 0u;
-        bar_named(1, kEpiW * 32);
-        if (*last_flag) {
-          __threadfence();
-          const PatchMap pm{it.b, it.x0, it.y0, tw, th, OH, OW};
-          epilogue_reduce<T>(ea, part, p.ksplit, tile_elems, n_tile, n_tile, it.nt * n_tile, pm, e, kEpiW);
-          if (warp == kEpiWarp0 && lane == 0) p.cnt[it.id] = 0;  // ready for the next launch
-        }
-        bar_named(1, kEpiW * 32);  // last_flag is rewritten for the next unit
       }
     }
   }
@@ -528,6 +519,39 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
   if (warp == 0) tmem_dealloc(tmem, p.tmem_cols);
 }
 
+
+// Split-K reduction of a k_tc_dw launch: item = blockIdx.x, its (8-row,
+// 16-column) units spread over every warp of gridDim.y CTAs. The partials are
+// summed in split order (reduce_units), so the result does not depend on how
+// the launches were scheduled; bias, residual, activation and the store
+// follow as in the unsplit epilogue.
+template <typename T>
+__global__ void __launch_bounds__(256) k_splitk_reduce(const EpiArgs a, const float *__restrict__ ws, int ksplit,
+                                                       int tiles_x, int tiles_y, int n_tiles, int tw, int th) {
+  pdl_trigger();
+  pdl_wait();  // the partials are the previous kernel's output
+  const int t = blockIdx.x;
+  const int nt = t % n_tiles;
+  int q = t / n_tiles;
+  const int tx = q % tiles_x;
+  q /= tiles_x;
+  const int ty = q % tiles_y;
+  const int b = q / tiles_y;
+  const PatchMap pm{b, tx * tw, ty * th, tw, th, a.OH, a.OW};
+  const size_t tile_elems = (size_t)kTileM * a.n_tile;
+  // the tile's bias, staged with scalar loads (the weight buffer's alignment is 4 bytes)
+  __shared__ __align__(16) float sbias[256];
+  for (int c = threadIdx.x; c < a.n_tile; c += blockDim.x) {
+    const int n = nt * a.n_tile + c;
+    sbias[c] = n < a.N ? a.bias[n] : 0.0f;
+  }
+  __syncthreads();
+  EpiArgs ea = a;
+  ea.bias = sbias;
+  const int wi = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5), nw = gridDim.y * (blockDim.x >> 5);
+  epilogue_reduce<T>(ea, ws + (size_t)t * ksplit * tile_elems, ksplit, tile_elems, a.n_tile, a.n_tile,
+                     nt * a.n_tile, pm, wi, nw);
+}
 
 constexpr size_t kSmemBudget = 227 * 1024;
 
@@ -544,7 +568,13 @@ cudaError_t launch_dw(const CUtensorMap &map, const CUtensorMap &map_out, const 
     granted |= 1ull << dev;
   }
   const unsigned grid = (unsigned)(p.total < sm_count() ? p.total : sm_count());
-  return launch_pdl(kern, dim3(grid), dim3(tcd::kThreads), smem, st, map, map_out, p);
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(tcd::kThreads), smem, st, map, map_out, p);
+  if (e != cudaSuccess || !SPLIT) return e;
+  // one warp per (8-row, 16-column) unit of an item
+  const int units = ((p.th * p.tw + 7) / 8) * ((p.epi.n_tile + kEpiCols - 1) / kEpiCols);
+  EpiArgs ea = p.epi;
+  return launch_pdl(k_splitk_reduce<T>, dim3((unsigned)p.items, (unsigned)((units + 7) / 8)), dim3(256), 0, st, ea,
+                    (const float *)p.ws, p.ksplit, p.tiles_x, p.tiles_y, p.n_tiles, p.tw, p.th);
 }
 
 template <typename T, int KS, int S, bool SPLIT>

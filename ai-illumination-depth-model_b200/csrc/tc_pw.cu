@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     fence_barrier_init();
   }
   if (tid == 0) pdl_trigger();
-  for (int i = tid; i < p.epi.N; i += kThreads) bias_smem[i] = p.epi.bias[i];
+  if (tid == 32) prefetch_tmap(&tmap_a), prefetch_tmap(&tmap_out);
   if (warp == 0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
   __syncthreads();
@@ -311,6 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     ea.bias = bias_smem;
     ea.cs = nullptr;
     ea.cs_ld = p.cs_ld;
+    // the bias is staged here, off the CTA's set-up path (only the epilogue reads it)
+    for (int i = tid - kEpiWarp0 * 32; i < p.epi.N; i += kEpiWarps * 32) bias_smem[i] = p.epi.bias[i];
+    bar_named(1, kEpiWarps * 32);
     pdl_wait();  // residual / coarse reads and the stores follow the previous kernel
     // per-warp TMA stores of whole 16-column slices, unless a warp's column
     // half is not a multiple of 16 (a slice would spill into the other half)
