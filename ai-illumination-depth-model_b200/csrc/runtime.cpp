@@ -355,6 +355,7 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
         g.act = op.act;
         g.OH = so.h, g.OW = so.w;
         g.M = (long)n * so.h * so.w;
+        g.ws = m.d_splitk, g.ws_bytes = m.d_splitk ? kSplitKBytes : 0;  // split-K partials (pw, dw->pw)
         if (op.kind == OpKind::Lateral) {
           const TensorShape &ss = a.shape(op.skip);
           g.mode = 2;
@@ -372,7 +373,6 @@ int enqueue_forward(illumina_model &m, int n, const float *frames, int layout, f
             g.ks = op.k, g.stride = op.stride;
             g.mid_act = op.mid_act;
             g.dw_w = w.dw_w, g.dw_b = w.dw_b;
-            g.ws = m.d_splitk, g.ws_bytes = m.d_splitk ? kSplitKBytes : 0;
             if ((int)i + 1 == m.head_fused_op) {
               // the head that reads this op's output runs in its epilogue
               const OpWeights &hw = m.opw[i + 1];
@@ -847,11 +847,8 @@ void op_gemm(const gpu::GemmOp &g, cudaStream_t st, const char *what) {
   Scratch img(plan.bytes, st);
   cuda_check(cudaMemsetAsync(img.p, 0, plan.bytes, st), "clear weight images");
   cuda_check(gpu::tc_pack(gpu::F32, g.w, g.N, g.K, plan, (uint8_t *)img.p, st), "pack weight images");
-  if (g.mode != 1) {
-    cuda_check(gpu::tc_op(gpu::F32, g, plan, (const uint8_t *)img.p, nullptr, st), what);
-    return;
-  }
-  cuda_check(gpu::tc_pack_dw(gpu::F32, g.dw_w, g.dw_b, plan, (uint8_t *)img.p, st), "pack depthwise blocks");
+  if (g.mode == 1)
+    cuda_check(gpu::tc_pack_dw(gpu::F32, g.dw_w, g.dw_b, plan, (uint8_t *)img.p, st), "pack depthwise blocks");
   Scratch ws(kSplitKOpBytes, st);
   gpu::GemmOp gs = g;
   gs.ws = (float *)ws.p, gs.ws_bytes = kSplitKOpBytes;

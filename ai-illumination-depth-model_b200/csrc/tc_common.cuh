@@ -10,6 +10,7 @@
 #include <cstdint>
 
 #include "arith.cuh"
+#include "pdl.cuh"
 
 namespace illumina {
 namespace gpu {
@@ -518,6 +519,41 @@ __device__ __noinline__ void epilogue_reduce(const EpiArgs a, const float *part,
     case 3: reduce_units<T, 3>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
     default: reduce_units<T, 0>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
   }
+}
+
+// Split-K reduction launched after a k_tc_dw or k_tc_pw launch that split K:
+// item = blockIdx.x (frame, tiles_x x tiles_y patch grid of tw x th pixels,
+// n tile; a pointwise item is a 128 x 1 patch of a 1 x M image), its (8-row,
+// 16-column) units spread over every warp of gridDim.y CTAs. The partials are
+// summed in split order (reduce_units), so the result does not depend on how
+// the launches were scheduled; bias, residual, activation and the store
+// follow as in the unsplit epilogue.
+template <typename T>
+__global__ void __launch_bounds__(256) k_splitk_reduce(const EpiArgs a, const float *__restrict__ ws, int ksplit,
+                                                       int tiles_x, int tiles_y, int n_tiles, int tw, int th) {
+  pdl_trigger();
+  pdl_wait();  // the partials are the previous kernel's output
+  const int t = blockIdx.x;
+  const int nt = t % n_tiles;
+  int q = t / n_tiles;
+  const int tx = q % tiles_x;
+  q /= tiles_x;
+  const int ty = q % tiles_y;
+  const int b = q / tiles_y;
+  const PatchMap pm{b, tx * tw, ty * th, tw, th, a.OH, a.OW};
+  const size_t tile_elems = (size_t)kTileM * a.n_tile;
+  // the tile's bias, staged with scalar loads (the weight buffer's alignment is 4 bytes)
+  __shared__ __align__(16) float sbias[256];
+  for (int c = threadIdx.x; c < a.n_tile; c += blockDim.x) {
+    const int n = nt * a.n_tile + c;
+    sbias[c] = n < a.N ? a.bias[n] : 0.0f;
+  }
+  __syncthreads();
+  EpiArgs ea = a;
+  ea.bias = sbias;
+  const int wi = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5), nw = gridDim.y * (blockDim.x >> 5);
+  epilogue_reduce<T>(ea, ws + (size_t)t * ksplit * tile_elems, ksplit, tile_elems, a.n_tile, a.n_tile,
+                     nt * a.n_tile, pm, wi, nw);
 }
 
 __device__ __forceinline__ void bar_named(int id, int n);

@@ -520,39 +520,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_dw(const __grid_constant__ C
 }
 
 
-// Split-K reduction of a k_tc_dw launch: item = blockIdx.x, its (8-row,
-// 16-column) units spread over every warp of gridDim.y CTAs. The partials are
-// summed in split order (reduce_units), so the result does not depend on how
-// the launches were scheduled; bias, residual, activation and the store
-// follow as in the unsplit epilogue.
-template <typename T>
-__global__ void __launch_bounds__(256) k_splitk_reduce(const EpiArgs a, const float *__restrict__ ws, int ksplit,
-                                                       int tiles_x, int tiles_y, int n_tiles, int tw, int th) {
-  pdl_trigger();
-  pdl_wait();  // the partials are the previous kernel's output
-  const int t = blockIdx.x;
-  const int nt = t % n_tiles;
-  int q = t / n_tiles;
-  const int tx = q % tiles_x;
-  q /= tiles_x;
-  const int ty = q % tiles_y;
-  const int b = q / tiles_y;
-  const PatchMap pm{b, tx * tw, ty * th, tw, th, a.OH, a.OW};
-  const size_t tile_elems = (size_t)kTileM * a.n_tile;
-  // the tile's bias, staged with scalar loads (the weight buffer's alignment is 4 bytes)
-  __shared__ __align__(16) float sbias[256];
-  for (int c = threadIdx.x; c < a.n_tile; c += blockDim.x) {
-    const int n = nt * a.n_tile + c;
-    sbias[c] = n < a.N ? a.bias[n] : 0.0f;
-  }
-  __syncthreads();
-  EpiArgs ea = a;
-  ea.bias = sbias;
-  const int wi = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5), nw = gridDim.y * (blockDim.x >> 5);
-  epilogue_reduce<T>(ea, ws + (size_t)t * ksplit * tile_elems, ksplit, tile_elems, a.n_tile, a.n_tile,
-                     nt * a.n_tile, pm, wi, nw);
-}
-
 constexpr size_t kSmemBudget = 227 * 1024;
 
 template <typename T, int KS, int S, int P, bool SPLIT>

@@ -23,6 +23,7 @@
 // leaves its loop; all roles meet before TMEM is released.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "kernels.h"
@@ -52,7 +53,25 @@ struct Params {
   int cs_ld;           // lateral: row stride (floats) of the coarse ring's tiles
   int cs_stages;       // lateral: coarse ring depth (0: the epilogue gathers the taps itself)
   uint32_t cs_bytes;   // cs_stages * 128 * cs_ld * 4
+  // split-K (pointwise only): unit u = tile * ksplit + split covers slabs
+  // [split * spk, min((split + 1) * spk, slabs)) and stores its fp32 partial
+  // tile at ws[(tile * ksplit + split) * 128 * n_tile]
+  int ksplit, spk;
+  float *ws;
 };
+
+// Tile (m tile, n tile) and slab range of work unit t.
+template <bool SPLIT>
+__device__ __forceinline__ void unit_of(const Params &p, int t, int &mt, int &nt, int &s0, int &s1) {
+  int tile = t;
+  s0 = 0, s1 = p.slabs;
+  if (SPLIT) {
+    tile = t / p.ksplit;
+    s0 = (t - tile * p.ksplit) * p.spk;
+    s1 = min(s0 + p.spk, p.slabs);
+  }
+  mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
+}
 
 // Lateral: the bilinear 2x upsample (refUpsample2, reference.ts:161-193:
 // source coordinate (i + 0.5) / 2 - 0.5, both taps from the unclamped floor,
@@ -140,8 +159,9 @@ __device__ __forceinline__ void coarse_tile(const EpiArgs &a, long M, long m0, i
   }
 }
 
-// MODE 0 pointwise, 2 lateral.
-template <typename T, int MODE>
+// MODE 0 pointwise, 2 lateral; SPLIT: the launch splits K (pointwise only)
+// and the epilogue stores fp32 partial tiles for k_splitk_reduce.
+template <typename T, int MODE, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ CUtensorMap tmap_a,
                                                        const __grid_constant__ CUtensorMap tmap_out, const Params p) {
   constexpr bool kF32 = sizeof(T) == 4;
@@ -190,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int total = p.m_tiles * p.n_tiles;
+  const int total = p.m_tiles * p.n_tiles * (SPLIT ? p.ksplit : 1);
   bool ok = true;
   const long long lim = p.wait;
 
@@ -202,8 +222,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
       uint32_t phase = 0;
       long issued = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int mt = t / p.n_tiles, nt = t % p.n_tiles;
-        for (int s = 0; s < p.slabs; s++) {
+        int mt, nt, s0, s1;
+        unit_of<SPLIT>(p, t, mt, nt, s0, s1);
+        for (int s = s0; s < s1; s++) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, lim)) {
             ok = false;
             break;
@@ -236,7 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
         }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)acc * p.acc_stride;
-        for (int s = 0; s < p.slabs; s++) {
+        int mt_, nt_, s0, s1;
+        unit_of<SPLIT>(p, t, mt_, nt_, s0, s1);
+        (void)mt_, (void)nt_;
+        for (int s = s0; s < s1; s++) {
           if (!mbar_wait(&full[stage], phase, lim) || (kF32 && !mbar_wait(&lo_rdy[stage], phase, lim))) {
             ok = false;
             break;
@@ -244,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
           tc_fence_after();
           const uint32_t sa = smem_u32(base + stage * stage_bytes);
           const uint32_t sb = sa + kTerms * kAImage;
-          mma_slab<kF32>(d, sa, sa + kAImage, sb, sb + b_img, idesc, s == 0);
+          mma_slab<kF32>(d, sa, sa + kAImage, sb, sb + b_img, idesc, s == s0);
           mma_commit(&empty[stage]);
           if (++stage == S) stage = 0, phase ^= 1u;
         }
@@ -265,7 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     if (ring) pdl_wait();  // the coarse map is an earlier kernel's output
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       if (kF32) {
-        for (int s = 0; s < p.slabs; s++) {
+        int mt_, nt_, s0, s1;
+        unit_of<SPLIT>(p, t, mt_, nt_, s0, s1);
+        (void)mt_, (void)nt_;
+        for (int s = s0; s < s1; s++) {
           if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, lim))) {
             ok = false;
             break;
@@ -322,7 +349,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_pw(const __grid_constant__ C
     uint8_t *wbuf = reinterpret_cast<uint8_t *>(epi_smem) + e * 2 * kWarpSliceBytes;
     float *blk = epi_smem + e * 32 * kEpiStride;
     uint32_t blocks = 0;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+    if (SPLIT) {
+      // each warp stores its lane quarter x column half of the partial tile
+      const size_t tile_elems = (size_t)kTileM * n_tile;
+      const int col0 = (e >> 2) * half;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int mt, nt, s0, s1;
+        unit_of<SPLIT>(p, t, mt, nt, s0, s1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, lim))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const long rows = p.M - (long)mt * kTileM;
+        store_partial(tmem + (uint32_t)acc * p.acc_stride + ((uint32_t)lane_base << 16) + (uint32_t)col0, lane_base,
+                      half, p.ws + (size_t)t * tile_elems + col0, n_tile, rows < kTileM ? (int)rows : kTileM);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (++acc == 2) acc = 0, acc_phase ^= 1u;
+      }
+    }
+    for (int t = blockIdx.x; t < total && ok && !SPLIT; t += gridDim.x) {
       const int mt = t / p.n_tiles, nt = t % p.n_tiles;
       const long m0 = (long)mt * kTileM;
       const long M = p.M;
@@ -421,11 +469,12 @@ int sm_count() {
 namespace {
 
 constexpr size_t kSmemBudget = 227 * 1024;
+constexpr int kSplitMinSlabs = 10;  // shortest K walk (in 128-byte slabs) that split-K shortens enough
 
-template <typename T, int MODE>
+template <typename T, int MODE, bool SPLIT>
 cudaError_t launch(const CUtensorMap &map, const CUtensorMap &map_out, const tcp::Params &p, size_t smem,
                    cudaStream_t st) {
-  auto kern = tcp::k_tc_pw<T, MODE>;
+  auto kern = tcp::k_tc_pw<T, MODE, SPLIT>;
   static unsigned long long granted = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -435,8 +484,17 @@ cudaError_t launch(const CUtensorMap &map, const CUtensorMap &map_out, const tcp
     granted |= 1ull << dev;
   }
   const long tiles = (long)p.m_tiles * p.n_tiles;
-  const unsigned grid = (unsigned)(tiles < sm_count() ? tiles : sm_count());
-  return launch_pdl(kern, dim3(grid), dim3(tcp::kThreads), smem, st, map, map_out, p);
+  const long units = tiles * (SPLIT ? p.ksplit : 1);
+  const unsigned grid = (unsigned)(units < sm_count() ? units : sm_count());
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(tcp::kThreads), smem, st, map, map_out, p);
+  if (e != cudaSuccess || !SPLIT) return e;
+  // the partials of each (m tile, n tile) item, summed in split order: an item
+  // is a run of 128 pixels, one 128 x 1 "patch" of a 1 x M image
+  tcx::EpiArgs ea = p.epi;
+  ea.OH = 1, ea.OW = (int)p.M;
+  const int red_units = (tcx::kTileM / 8) * ((p.epi.n_tile + tcx::kEpiCols - 1) / tcx::kEpiCols);
+  return launch_pdl(tcx::k_splitk_reduce<T>, dim3((unsigned)tiles, (unsigned)((red_units + 7) / 8)), dim3(256), 0,
+                    st, ea, (const float *)p.ws, p.ksplit, p.m_tiles, 1, p.n_tiles, tcx::kTileM, 1);
 }
 
 }  // namespace
@@ -503,9 +561,36 @@ cudaError_t tc_pw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   if (stages > 6) stages = 6;
   if (stages < 2) return cudaErrorInvalidValue;
   p.stages = stages;
+  // split-K when the launch has too few tiles to occupy the SMs and the tile's
+  // K walk is long (pointwise only): each split takes spk slabs of the tile and
+  // the partials fit the workspace. The reduction is a second launch, which at
+  // small batches costs about as much as 6-8 slabs of one tile's serial walk
+  // (measured), so shorter K walks are not split.
+  p.ksplit = 1, p.spk = plan.slabs, p.ws = nullptr;
+  {
+    const long tiles = (long)p.m_tiles * p.n_tiles;
+    const double tile_bytes = (double)tcx::kTileM * plan.n_tile * 4;
+    if (op.mode == 0 && op.ws && plan.slabs >= kSplitMinSlabs && tiles * 2 <= sm_count()) {
+      int want = (int)std::min<long>(plan.slabs, std::max<long>(1, sm_count() / tiles));
+      for (; want > 1; want--) {
+        const int spk = (plan.slabs + want - 1) / want, ks = (plan.slabs + spk - 1) / spk;
+        if (tiles * ks * tile_bytes <= (double)op.ws_bytes) {
+          p.spk = spk, p.ksplit = ks;
+          break;
+        }
+      }
+    }
+    if (p.ksplit > 1) p.ws = op.ws;
+  }
   const size_t smem = stages * stage + 1024 + tcp::kEpiPw + p.bias_bytes + p.cs_bytes + 8 * (3 * stages + 9) + 16;
-  if (T == F32) return op.mode == 0 ? launch<float, 0>(map, map_out, p, smem, st) : launch<float, 2>(map, map_out, p, smem, st);
-  return op.mode == 0 ? launch<__nv_bfloat16, 0>(map, map_out, p, smem, st) : launch<__nv_bfloat16, 2>(map, map_out, p, smem, st);
+  const bool split = p.ksplit > 1;
+  if (T == F32) {
+    if (op.mode == 2) return launch<float, 2, false>(map, map_out, p, smem, st);
+    return split ? launch<float, 0, true>(map, map_out, p, smem, st) : launch<float, 0, false>(map, map_out, p, smem, st);
+  }
+  if (op.mode == 2) return launch<__nv_bfloat16, 2, false>(map, map_out, p, smem, st);
+  return split ? launch<__nv_bfloat16, 0, true>(map, map_out, p, smem, st)
+               : launch<__nv_bfloat16, 0, false>(map, map_out, p, smem, st);
 }
 
 }  // namespace gpu

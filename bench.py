@@ -485,7 +485,7 @@ def source_sampling(model, stream, ev0, ev1, batch=64, reps=10):
             "source": f"{w}x{h} RGBA8, centre crop, bilinear clamp-to-edge", "output": "3x448x448 f32 planar"}
 
 
-def batch_sweep(model, frames, disp, stream, ev0, ev1, batches=(1, 8, 64, 256)):
+def batch_sweep(model, frames, disp, stream, ev0, ev1, batches=(1, 8, 64, 256), reps=None):
     """Latency and frames/s of one forward at each batch size (device-resident
     blob frames; batch b takes consecutive slices of the 256 generated frames
     in turn, so small batches do not re-read L2-resident inputs)."""
@@ -496,16 +496,16 @@ def batch_sweep(model, frames, disp, stream, ev0, ev1, batches=(1, 8, 64, 256)):
         if b > n:
             continue
         views = [(frames[i:i + b], disp[i:i + b]) for i in range(0, n - b + 1, b)]
-        reps = max(5, min(200, 2048 // b))
+        n_reps = reps or max(5, min(200, 2048 // b))
         for k in range(min(len(views), 8) + 3):
             model.forward(views[k % len(views)][0], disparity=views[k % len(views)][1], stream=stream)
         torch.cuda.synchronize()
         ev0.record(stream)
-        for k in range(reps):
+        for k in range(n_reps):
             model.forward(views[k % len(views)][0], disparity=views[k % len(views)][1], stream=stream)
         ev1.record(stream)
         torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1) / reps
+        ms = ev0.elapsed_time(ev1) / n_reps
         out.append({"batch": b, "latency_ms": ms, "frames_per_s": b * 1000.0 / ms, "us_per_frame": 1000.0 * ms / b})
     return out
 
@@ -792,7 +792,7 @@ def run_only(args, local_rank):
             out = depth_relight_frame(model, frames, ring, stream, ev0, ev1, reps=args.steps)
         else:
             disp = torch.empty((ring, SIZE, SIZE), dtype=torch.float32, device="cuda")
-            out = batch_sweep(model, frames, disp, stream, ev0, ev1, batches=(args.batch,))
+            out = batch_sweep(model, frames, disp, stream, ev0, ev1, batches=(args.batch,), reps=args.steps)
     model.destroy()
     print(json.dumps({args.only: out}), flush=True)
     return 0

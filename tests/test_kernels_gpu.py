@@ -163,3 +163,29 @@ def test_arith_helpers_exhaustive(which, name):
     _lib.check(_lib.lib().illumina_selftest(which, out))
     assert out[0] == (1 << 32) - 2 * ((1 << 23) - 1), name   # every pattern but the NaNs
     assert out[1] == 0, f"{name}: {out[1]} mismatches, e.g. input bits {out[2]:#010x}"
+
+
+@pytest.mark.parametrize("h,w,in_c,out_c,res", [(14, 14, 416, 176, False), (7, 9, 352, 24, True)])
+def test_pointwise_split_k_matches_oracle(torch, h, w, in_c, out_c, res):
+    """Pointwise ops with a long K walk and few 128-pixel tiles (the bottleneck
+    shapes at small batches) take the split-K path of the tensor engine: fp32
+    partials per K split, summed in split order by a reduction launch; compared
+    with the oracle at the kernel tolerance (2e-4 / 2e-3)."""
+    from illumina import _lib, ops
+    from oracle import reference as R
+    st = 0x5B17 + in_c
+    src, st = cases.random_floats(st, h * w * in_c, 1.0)
+    wt, st = cases.random_floats(st, out_c * in_c, 0.1)
+    b, st = cases.random_floats(st, out_c, 0.5)
+    r, st = cases.random_floats(st, h * w * out_c, 1.0)
+    want = R.pointwise(src, h, w, in_c, wt, b, out_c, "hardswish", r if res else None)
+    lib = _lib.lib()
+    lib.illumina_set_op_engine(_lib.ENGINE["tensor"])
+    try:
+        got = ops.pointwise(dev(torch, src), h, w, in_c, dev(torch, wt), dev(torch, b), out_c, "hardswish",
+                            dev(torch, r) if res else None)
+        torch.cuda.synchronize()
+    finally:
+        lib.illumina_set_op_engine(_lib.ENGINE["simt"])
+    _, _, worst = compare(got.cpu().numpy(), want, 2e-4, 2e-3)
+    assert worst == [], worst
