@@ -106,7 +106,7 @@ def test_network64_aliased_arena_live_at_end(torch, net64):
 
 
 def test_network448_single_frame_fp32(torch):
-    """448, seed-0 weights, uniform frame from seed 0."""
+    """The single-frame workload: 448, seed-0 weights, uniform frame from seed 0."""
     from oracle import arch as OA
     from oracle import reference as R
     from oracle import weights as OW

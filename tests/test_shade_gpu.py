@@ -180,7 +180,7 @@ def test_render_frame_and_skip_inference(torch):
 
 
 def test_config4_render_1080p_band_matches_oracle(torch):
-    """BASELINE config 4 geometry: 448 depth, 1920x1080 render, 4 seeded point lights,
+    """The relighting-frame geometry: 448 depth, 1920x1080 render, 4 seeded point lights,
     16 contact / 12 volumetric steps; compared on a band of rows (the oracle is scalar)."""
     from illumina.lighting import DEFAULT_SETTINGS
     from illumina.workloads import config4_lights
