@@ -214,7 +214,14 @@ __device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
   hi = tf32_round(x);
   lo = __float_as_uint(x - __uint_as_float(hi));
 }
-__device__ __forceinline__ float hardswish(float v) { return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)); }
+// hardswish in the tensor-core kernels: the division by 6 as one multiply by
+// RN(1/6), within 1.5 ulp of the quotient (RN(1/6) is within half an ulp of
+// 1/6, and the product is rounded once more) -- the accuracy class the
+// reference shader's WGSL division is specified to (2.5 ulp) -- at one
+// instruction instead of div6's four; these kernels are issue bound.
+__device__ __forceinline__ float hardswish(float v) {
+  return v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f) * (1.0f / 6.0f);
+}
 __device__ __forceinline__ float act_apply(int act, float v) {
   switch (act) {
     case 1: return fmaxf(v, 0.0f);
