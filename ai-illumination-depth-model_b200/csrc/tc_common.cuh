@@ -214,14 +214,21 @@ __device__ __forceinline__ void split(float x, uint32_t &hi, uint32_t &lo) {
   hi = tf32_round(x);
   lo = __float_as_uint(x - __uint_as_float(hi));
 }
-// hardswish in the tensor-core kernels: the division by 6 as one multiply by
-// RN(1/6), within 1.5 ulp of the quotient (RN(1/6) is within half an ulp of
-// 1/6, and the product is rounded once more) -- the accuracy class the
-// reference shader's WGSL division is specified to (2.5 ulp) -- at one
-// instruction instead of div6's four; these kernels are issue bound.
-__device__ __forceinline__ float hardswish(float v) {
+__device__ __forceinline__ float hardswish(float v) { return div6(v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f)); }
+// hardswish with the division by 6 as one multiply by RN(1/6): within 1.5 ulp
+// of the quotient (RN(1/6) is within half an ulp of 1/6, and the product is
+// rounded once more) -- the accuracy class the reference shader's WGSL
+// division is specified to (2.5 ulp) -- at one instruction instead of div6's
+// four; the tensor-core kernels are issue bound. fp32 storage only: RN(1/6)
+// is above 1/6, and where every layer's activations are re-rounded to bf16
+// that bias shifts the bf16 roundings through the network, so the BF16
+// instances keep div6.
+__device__ __forceinline__ float hardswish_fast(float v) {
   return v * fminf(fmaxf(v + 3.0f, 0.0f), 6.0f) * (1.0f / 6.0f);
 }
+// Compile-time id of hardswish for storage type T (see hardswish_fast).
+template <typename T>
+constexpr int kHswish = sizeof(T) == 4 ? 4 : 3;
 __device__ __forceinline__ float act_apply(int act, float v) {
   switch (act) {
     case 1: return fmaxf(v, 0.0f);
@@ -230,13 +237,15 @@ __device__ __forceinline__ float act_apply(int act, float v) {
     default: return v;
   }
 }
-// Compile-time activation (0 linear, 1 relu, 2 relu6, 3 hardswish) for loops
-// that dispatch on the activation once, outside the loop.
+// Compile-time activation (0 linear, 1 relu, 2 relu6, 3 hardswish, 4 the
+// single-multiply hardswish) for loops that dispatch on the activation once,
+// outside the loop.
 template <int ACT>
 __device__ __forceinline__ float act_c(float v) {
   if (ACT == 1) return fmaxf(v, 0.0f);
   if (ACT == 2) return fminf(fmaxf(v, 0.0f), 6.0f);
   if (ACT == 3) return hardswish(v);
+  if (ACT == 4) return hardswish_fast(v);
   return v;
 }
 template <int ACT>
@@ -523,7 +532,7 @@ __device__ __noinline__ void epilogue_reduce(const EpiArgs a, const float *part,
   switch (a.act) {
     case 1: reduce_units<T, 1>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
     case 2: reduce_units<T, 2>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
-    case 3: reduce_units<T, 3>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
+    case 3: reduce_units<T, kHswish<T>>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
     default: reduce_units<T, 0>(a, part, ksplit, split_stride, ld, ncols, n_base, pm, wi, nw); break;
   }
 }
@@ -689,7 +698,7 @@ __device__ __forceinline__ bool epilogue_tma(const EpiArgs &a, uint32_t tacc_lan
       return epilogue_tma_body<T, 2>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
                                      release, store);
     case 3:
-      return epilogue_tma_body<T, 3>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
+      return epilogue_tma_body<T, kHswish<T>>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
                                      release, store);
     default:
       return epilogue_tma_body<T, 0>(a, tacc_lane, row, ncols, n_base, m, bufs, slice, elected, bar_id, bar_n, ready,
@@ -760,7 +769,9 @@ __device__ __forceinline__ bool warp_tma_epilogue(const EpiArgs &a, uint32_t tac
   switch (a.act) {
     case 1: return warp_tma_body<T, 1>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
     case 2: return warp_tma_body<T, 2>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
-    case 3: return warp_tma_body<T, 3>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
+    case 3:
+      return warp_tma_body<T, kHswish<T>>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release,
+                                         store);
     default:
       return warp_tma_body<T, 0>(a, tacc_lane, col0, ncols, n_base, m, cs_row, wbuf, blocks, ready, release, store);
   }
@@ -791,7 +802,7 @@ __device__ __forceinline__ bool epilogue_rows(const EpiArgs &a, uint32_t tacc_la
   switch (a.act) {
     case 1: return epilogue_body<T, MODE, 1>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
     case 2: return epilogue_body<T, MODE, 2>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
-    case 3: return epilogue_body<T, MODE, 3>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
+    case 3: return epilogue_body<T, MODE, kHswish<T>>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
     default: return epilogue_body<T, MODE, 0>(a, tacc_lane, col0, ncols, n_base, blk, rows, ready);
   }
 }

@@ -201,7 +201,7 @@ __device__ __forceinline__ void depthwise_dispatch(const Params &p, const Item &
   switch (p.mid_act) {
     case 1: depthwise_slab<T, KS, S, P, 1>(p, it, halo, dww, A, ct, cgn); break;
     case 2: depthwise_slab<T, KS, S, P, 2>(p, it, halo, dww, A, ct, cgn); break;
-    case 3: depthwise_slab<T, KS, S, P, 3>(p, it, halo, dww, A, ct, cgn); break;
+    case 3: depthwise_slab<T, KS, S, P, kHswish<T>>(p, it, halo, dww, A, ct, cgn); break;
     default: depthwise_slab<T, KS, S, P, 0>(p, it, halo, dww, A, ct, cgn); break;
   }
 }
