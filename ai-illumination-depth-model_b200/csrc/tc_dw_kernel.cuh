@@ -8,16 +8,16 @@
 // channels); the patch's th*tw <= 128 pixels are the 128 rows of one UMMA
 // tile. Per item the kernel walks the input channels in 128-byte slabs.
 //
-// Roles inside one CTA (480 threads, one CTA per SM, items strided by grid):
+// Roles inside one CTA (640 threads, one CTA per SM, items strided by grid):
 //   warp 0        halo producer: per (item, slab) one 4-D TMA load of the
 //                 input halo ((th-1)*S+KS rows x (tw-1)*S+KS columns x one
 //                 slab, unswizzled; coordinates outside the frame read as
 //                 zero, which is the depthwise zero padding) plus a bulk copy
 //                 of the slab's depthwise taps and bias into the `H` ring.
-//   warp 14       weight producer: bulk copies of the pre-swizzled pointwise
+//   warp 2        weight producer: bulk copies of the pre-swizzled pointwise
 //                 weight images into the `G` ring, or once into a resident
 //                 region when all of the op's images fit in shared memory.
-//   warps 2-9     depthwise, in `ng` groups of four warps that take the
+//   warps 4-11    depthwise, in `ng` groups of four warps that take the
 //                 (item, slab) steps in turn (group g takes steps g, g+ng, ..),
 //                 so one group's shared-memory latency hides behind the
 //                 other's arithmetic. Each thread owns 4 channels of a run of
@@ -27,10 +27,10 @@
 //                 hi/lo pair for fp32 storage, bf16 for bf16 storage).
 //   warp 1        one thread issues tcgen05.mma into one of two TMEM
 //                 accumulators and commits each G stage back to the ring.
-//   warps 10-13   epilogue (tcx::epilogue_rows), one warp per TMEM lane
-//                 quarter: bias and residual loaded before the accumulator
-//                 is waited for, then activation and store; then release
-//                 the accumulator.
+//   warps 12-19   epilogue, two teams of four warps (one per TMEM
+//                 accumulator), one warp per TMEM lane quarter: bias and
+//                 residual loaded before the accumulator is waited for, then
+//                 activation and store; then release the accumulator.
 // A ring stage is always used by the same depthwise group (the ring depths
 // are multiples of ng), so a group's own previous use of a stage orders its
 // parity waits. Every mbarrier wait is bounded; a role that gives up records
