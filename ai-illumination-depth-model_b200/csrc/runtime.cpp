@@ -134,6 +134,10 @@ struct illumina_model {
   float *d_scene = nullptr;
   float *d_tex[2] = {nullptr, nullptr};
   float *d_stage_in = nullptr, *d_stage_out = nullptr, *d_stage_low = nullptr;
+  // 8-bit source images of a host-buffer illumina_forward_source that do not
+  // fit behind the planar frames in d_stage_in (allocated on first need)
+  uint8_t *d_src = nullptr;
+  size_t d_src_bytes = 0;
   size_t device_bytes = 0;
   int history_index = 0, last_written = 1;
   float exposure = 1, range_sigma = 0.12f, base_alpha = 0.35f, sensitivity = 3.0f;
@@ -182,6 +186,7 @@ illumina_model::~illumina_model() {
   cudaFree(d_stage_in);
   cudaFree(d_stage_out);
   cudaFree(d_stage_low);
+  cudaFree(d_src);
   cudaFree(d_wimg);
   if (h_err) cudaFreeHost((void *)h_err);
   cudaFree(d_splitk);
@@ -510,6 +515,31 @@ int host_chunks(int n, int *sizes) {
   return k;
 }
 
+// Chunk sizes for a host-buffer forward whose frames upload ~3x faster than
+// they compute (8-bit RGBA sources at the network resolution: ~15 us per
+// 448 frame at 55 GB/s against ~50 us of compute): a first chunk of 8 (the
+// only upload nothing overlaps), then chunks growing threefold while the
+// uploads stay ahead of the compute, a chunk of 48 whose compute hides the
+// largest chunk's download, and a last chunk of 8 (the only download nothing
+// overlaps). Below 160 frames the planar-frame schedule. A pipeline model fed
+// with the measured per-batch costs puts 8, 48, 144, 48, 8 within 1 % of the
+// best five-chunk schedule at 256 frames.
+int host_chunks_fast_upload(int n, int *sizes) {
+  if (n < 160) return host_chunks(n, sizes);
+  constexpr int kMax = illumina_model::kMaxChunks;
+  int k = 0, rem = n - 8 - 48 - 8, step = 48;
+  sizes[k++] = 8;
+  while (rem > 0) {
+    int c = std::min(step, rem);
+    if (rem - c < 48 || k == kMax - 3) c = rem;
+    sizes[k++] = c, rem -= c;
+    step = std::min(3 * step, 1024);
+  }
+  sizes[k++] = 48;
+  sizes[k++] = 8;
+  return k;
+}
+
 // Reports a bounded device wait that gave up (the kernels set the model's
 // error word and left the rest of their work undone, so the outputs of the
 // forward that ran them are undefined): clears the word and throws TIMEOUT.
@@ -543,6 +573,9 @@ void run_forward(illumina_model &m, const float *frames, int n, int layout, floa
 
   cuda_check(cudaEventRecord(m.ev_join, caller), "event record");
   cuda_check(cudaStreamWaitEvent(m.stream, m.ev_join, 0), "stream wait");
+  // the copy streams also wait for work queued on the model stream before
+  // this call (an asynchronous forward may still read the staging buffers)
+  cuda_check(cudaEventRecord(m.ev_join, m.stream), "event record");
 
   // Host buffers, whole batches: frame chunks, each uploaded on copy_in, run
   // through the (chunk-sized) graph on the model stream and downloaded on
@@ -622,6 +655,107 @@ void run_forward(illumina_model &m, const float *frames, int n, int layout, floa
   cuda_check(cudaEventRecord(m.ev_done, m.stream), "event record");
   cuda_check(cudaStreamWaitEvent(caller, m.ev_done, 0), "caller wait");
   if (sync) {
+    cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+    check_timeout(m, "in this call");
+  }
+}
+
+// The hot path from 8-bit RGBA source images (n x h x w x 4 bytes, host or
+// device), the reference's frame path: a camera or canvas frame uploaded as an
+// rgba8unorm texture and read by makePreprocess (src/model/kernels/io.ts:64-118)
+// at uv * uv_scale + uv_offset. Each frame chunk's bytes are uploaded on
+// copy_in, sampled to planar float frames on the model stream (the kernel of
+// illumina_sample_source) and run through the chunk's graph; the disparity
+// goes back on copy_out. A host source moves 4 bytes per source pixel over
+// PCIe instead of the 12 of planar float frames at the network resolution.
+void run_forward_source(illumina_model &m, const uint8_t *rgba8, int n, int w, int h, const float *uv_scale,
+                        const float *uv_offset, int mirror, float *disp, cudaStream_t caller) {
+  if (n < 1 || n > m.opts.max_batch)
+    throw Error(ILLUMINA_INVALID_ARG, "forwardSource: batch " + std::to_string(n) + " outside [1, " +
+                                          std::to_string(m.opts.max_batch) + "]");
+  if (w < 1 || h < 1 || (long)w * h > (1L << 26))
+    throw Error(ILLUMINA_INVALID_ARG, "forwardSource: source size " + std::to_string(w) + "x" + std::to_string(h) +
+                                          " outside [1, 2^26] pixels");
+  if (!rgba8) throw Error(ILLUMINA_INVALID_ARG, "forwardSource: rgba8 is null");
+  if ((reinterpret_cast<uintptr_t>(rgba8) & 3) != 0)
+    throw Error(ILLUMINA_INVALID_ARG, "forwardSource: rgba8 must be 4-byte aligned");
+  cuda_check(cudaSetDevice(m.device), "cudaSetDevice");
+  check_timeout(m, "in an earlier call on this model");
+  const int S = m.arch.input_size;
+  const long planar = 3L * S * S, disp_floats = (long)S * S;
+  const size_t src_bytes = (size_t)w * h * 4;
+  const float one[2] = {1.0f, 1.0f}, zero[2] = {0.0f, 0.0f};
+  const float *us = uv_scale ? uv_scale : one, *uo = uv_offset ? uv_offset : zero;
+  const bool host_in = !is_device_ptr(rgba8);
+  const bool host_disp = disp && !is_device_ptr(disp);
+
+  // a host source is staged behind the planar frames in d_stage_in (sized for
+  // the interleaved RGBA layout: 4 floats per pixel) when it fits there
+  const uint8_t *stage = nullptr;
+  if (host_in) {
+    const size_t tail = sizeof(float) * (size_t)m.opts.max_batch * (4L * S * S - planar);
+    if (src_bytes * n <= tail) {
+      stage = reinterpret_cast<uint8_t *>(m.d_stage_in + (size_t)m.opts.max_batch * planar);
+    } else {
+      if (m.d_src_bytes < src_bytes * n) {
+        cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+        cudaFree(m.d_src);
+        m.d_src = nullptr, m.d_src_bytes = 0;
+        cuda_check(cudaMalloc(&m.d_src, src_bytes * n), "cudaMalloc source staging");
+        m.d_src_bytes = src_bytes * n;
+      }
+      stage = m.d_src;
+    }
+  }
+
+  cuda_check(cudaEventRecord(m.ev_join, caller), "event record");
+  cuda_check(cudaStreamWaitEvent(m.stream, m.ev_join, 0), "stream wait");
+  // the copy streams also wait for work queued on the model stream before
+  // this call (an asynchronous forward may still read the staging buffers)
+  cuda_check(cudaEventRecord(m.ev_join, m.stream), "event record");
+  cuda_check(cudaStreamWaitEvent(m.copy_in, m.ev_join, 0), "stream wait");
+  cuda_check(cudaStreamWaitEvent(m.copy_out, m.ev_join, 0), "stream wait");
+  int sizes[illumina_model::kMaxChunks], chunks = 1;
+  if (host_in || host_disp)
+    // sources of at most a third of a planar float frame's bytes upload fast
+    chunks = host_in && src_bytes * 3 <= sizeof(float) * planar ? host_chunks_fast_upload(n, sizes)
+                                                                : host_chunks(n, sizes);
+  else
+    sizes[0] = n;
+  long starts[illumina_model::kMaxChunks];
+  for (int k = 0, f = 0; k < chunks; f += sizes[k], k++) starts[k] = f;
+  if (host_in)
+    for (int k = 0; k < chunks; k++) {
+      cuda_check(cudaMemcpyAsync(const_cast<uint8_t *>(stage) + starts[k] * src_bytes, rgba8 + starts[k] * src_bytes,
+                                 src_bytes * sizes[k], cudaMemcpyHostToDevice, m.copy_in),
+                 "source H2D");
+      cuda_check(cudaEventRecord(m.ev_in[k], m.copy_in), "event record");
+    }
+  for (int k = 0; k < chunks; k++) {
+    const long f0 = starts[k];
+    const int nk = sizes[k];
+    if (host_in) cuda_check(cudaStreamWaitEvent(m.stream, m.ev_in[k], 0), "stream wait");
+    float *frames = m.d_stage_in + f0 * planar;
+    cuda_check(gpu::sample_source((host_in ? stage : rgba8) + f0 * src_bytes, nk, w, h, us, uo, mirror ? 1 : 0, S,
+                                  frames, m.stream),
+               "sample_source");
+    float *d_disp = (host_disp || !disp ? m.d_stage_out : disp) + f0 * disp_floats;
+    GraphKey key{nk, ILLUMINA_FRAME_RGB_PLANAR, 0, 0, nullptr, nullptr};
+    GraphEntry &g = graph_for(m, key, frames, d_disp, nullptr, nullptr, nullptr);
+    cuda_check(cudaGraphLaunch(g.exec, m.stream), "graph launch");
+    if (host_disp) {
+      cuda_check(cudaEventRecord(m.ev_fwd[k], m.stream), "event record");
+      cuda_check(cudaStreamWaitEvent(m.copy_out, m.ev_fwd[k], 0), "stream wait");
+      cuda_check(cudaMemcpyAsync(disp + f0 * disp_floats, d_disp, sizeof(float) * nk * disp_floats,
+                                 cudaMemcpyDeviceToHost, m.copy_out),
+                 "disparity D2H");
+    }
+  }
+  cuda_check(cudaEventRecord(m.ev_out, m.copy_out), "event record");
+  cuda_check(cudaStreamWaitEvent(m.stream, m.ev_out, 0), "stream wait");
+  cuda_check(cudaEventRecord(m.ev_done, m.stream), "event record");
+  cuda_check(cudaStreamWaitEvent(caller, m.ev_done, 0), "caller wait");
+  if (host_in || host_disp) {
     cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
     check_timeout(m, "in this call");
   }
@@ -995,6 +1129,16 @@ illumina_status illumina_forward(illumina_model *m, const float *frames, int n, 
   ILL_TRY
   require(m, "forward: null model");
   run_forward(*m, frames, n, layout, disparity, depth_low, (cudaStream_t)stream, 0);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_forward_source(illumina_model *m, const uint8_t *rgba8, int n, int src_w, int src_h,
+                                        const float *uv_scale, const float *uv_offset, int mirror, float *disparity,
+                                        void *stream) {
+  ILL_TRY
+  require(m, "forwardSource: null model");
+  run_forward_source(*m, rgba8, n, src_w, src_h, uv_scale, uv_offset, mirror, disparity, (cudaStream_t)stream);
   return ILLUMINA_OK;
   ILL_CATCH
 }

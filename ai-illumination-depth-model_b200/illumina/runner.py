@@ -127,9 +127,34 @@ class DepthModel:
         return frames
 
     def forwardSource(self, rgba8, uvScale=None, uvOffset=None, mirror: bool = False, disparity=None, stream=None):
-        """forward() on 8-bit source images: sampleSource, then the hot path."""
-        frames = self.sampleSource(rgba8, uvScale, uvOffset, mirror, stream=stream)
-        return self.forward(frames, disparity=disparity, stream=stream)
+        """forward() on 8-bit RGBA source images [n, h, w, 4] (numpy uint8 on the host or a CUDA
+        uint8 tensor): the source read of makePreprocess, then the hot path, in one call
+        (illumina_forward_source). Returns the disparity [n, S, S] (numpy for a host source,
+        a CUDA tensor for a device source, or `disparity` when given)."""
+        host = not _is_torch(rgba8)
+        if host:
+            rgba8 = np.ascontiguousarray(rgba8, np.uint8)
+        else:
+            import torch
+            if rgba8.dtype != torch.uint8 or not rgba8.is_cuda or not rgba8.is_contiguous():
+                raise ValueError("rgba8 must be a contiguous uint8 array or CUDA tensor [n, h, w, 4]")
+        if rgba8.ndim == 3:
+            rgba8 = rgba8[None]
+        if rgba8.shape[-1] != 4:
+            raise ValueError(f"rgba8 must be [n, h, w, 4], got {list(rgba8.shape)}")
+        n, h, w = int(rgba8.shape[0]), int(rgba8.shape[1]), int(rgba8.shape[2])
+        S = self.arch.inputSize
+        if disparity is None:
+            if host:
+                disparity = np.empty((n, S, S), np.float32)
+            else:
+                import torch
+                disparity = torch.empty((n, S, S), dtype=torch.float32, device=rgba8.device)
+        sc = (C.c_float * 2)(*(uvScale if uvScale is not None else self.uvScale))
+        of = (C.c_float * 2)(*(uvOffset if uvOffset is not None else self.uvOffset))
+        check(lib().illumina_forward_source(self._h, ptr(rgba8), n, w, h, sc, of, int(bool(mirror)), ptr(disparity),
+                                            stream_handle(stream)))
+        return disparity
 
     def record(self, frame, stream=None):
         """record (runner.ts:440-449): one streaming frame blended with the temporal history."""

@@ -163,6 +163,23 @@ illumina_status illumina_model_set_temporal(illumina_model *model, float base_al
 illumina_status illumina_forward(illumina_model *model, const float *frames, int n, int frame_layout,
                                  float *disparity, float *depth_low, void *stream);
 
+/* The hot path from 8-bit RGBA source images, the reference's frame path: a
+ * camera or canvas frame uploaded as an rgba8unorm texture (src/main.ts,
+ * src/scene/blit.ts) and read by makePreprocess (kernels/io.ts:64-118).
+ * `rgba8`: n images of src_h x src_w x 4 bytes, host or device, 4-byte
+ * aligned; sampled as illumina_sample_source does (uv_scale / uv_offset
+ * nullable: (1,1) / (0,0); `mirror` flips u), then illumina_forward on the
+ * sampled planar frames. `disparity` (host, device or NULL) receives
+ * n x S x S float32. With host buffers the call is synchronous and runs in
+ * frame chunks whose uploads, sampling, graphs and downloads overlap; a host
+ * source moves 4 bytes per source pixel over PCIe, against 12 per network
+ * pixel for planar float frames. A host source larger than the model's
+ * staging room (max_batch x S x S x 4 bytes) is staged in a device buffer the
+ * model allocates on first need. ILLUMINA_TIMEOUT as for illumina_forward. */
+illumina_status illumina_forward_source(illumina_model *model, const uint8_t *rgba8, int n, int src_w, int src_h,
+                                        const float *uv_scale, const float *uv_offset, int mirror, float *disparity,
+                                        void *stream);
+
 /* forwardReference from a given network input (scripts/ref-forward.ts:296-300,
  * an "input" bundle; src/model/reference.ts:360-451): `input` holds n x S x S x 4
  * float32 channels-last preprocess outputs (host or device). Runs the stem as

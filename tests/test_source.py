@@ -119,3 +119,70 @@ def test_sample_source_rejects_bad_arguments(torch):
     assert "aligned" in lib.illumina_last_error().decode()
     assert lib.illumina_sample_source(None, 1, 4, 4, None, None, 0, 32, frames.data_ptr(), None) != 0
     del illumina
+
+
+def _device_path(torch, model, rgba8, scale, offset, mirror):
+    """sampleSource + forward on device buffers: the unchunked reference for the host path."""
+    frames = model.sampleSource(torch.from_numpy(rgba8).cuda(), scale, offset, mirror)
+    disp = model.forward(frames)
+    torch.cuda.synchronize()
+    return disp.cpu().numpy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("sw,sh,mirror", [(64, 64, False), (96, 80, True)])
+def test_forward_source_host_chunks_bitwise(torch, sw, sh, mirror):
+    """illumina_forward_source with host RGBA8 frames and a host disparity buffer: 40
+    frames run as overlapped chunks (uploads, sampling, graphs, downloads); the
+    96x80 source does not fit the staging room behind the planar frames and goes
+    through the model's own source buffer. Equal to sampling and
+    forwarding the whole batch on device buffers within the whole-network tolerance
+    (1e-5), and bit-identical across calls."""
+    import illumina
+    S, n = 64, 40
+    rng = np.random.default_rng(sw + sh)
+    px = rng.integers(0, 256, (n, sh, sw, 4), dtype=np.uint8)
+    scale, offset = (0.9, 0.8), (0.05, 0.1)
+    model = illumina.createDepthModel(illumina.buildArchitecture(S), synthSeed=cases.NET64_SEED, maxBatch=n)
+    got = model.forwardSource(px, scale, offset, mirror)
+    got2 = model.forwardSource(px, scale, offset, mirror)  # second call: staging and graphs reused
+    want = _device_path(torch, model, px, scale, offset, mirror)
+    assert model.stats.deviceError == 0
+    model.destroy()
+    assert got.shape == (n, S, S)
+    np.testing.assert_array_equal(got2, got)
+    # a chunk's forward equals a forward of those frames alone; the whole-batch
+    # forward may split K differently (its own summation order)
+    assert float(np.abs(got - want).max()) <= 1e-5
+
+
+@pytest.mark.gpu
+def test_forward_source_device_buffers(torch):
+    """Device RGBA8 in, device disparity out: one asynchronous call, equal to the host path."""
+    import illumina
+    S, n = 64, 3
+    px = np.random.default_rng(7).integers(0, 256, (n, S, S, 4), dtype=np.uint8)
+    model = illumina.createDepthModel(illumina.buildArchitecture(S), synthSeed=cases.NET64_SEED, maxBatch=n)
+    dev = model.forwardSource(torch.from_numpy(px).cuda())
+    torch.cuda.synchronize()
+    host = model.forwardSource(px)
+    model.destroy()
+    np.testing.assert_array_equal(dev.cpu().numpy(), host)
+
+
+@pytest.mark.gpu
+def test_forward_source_rejects_bad_arguments(torch):
+    import illumina
+    from illumina import _lib
+    model = illumina.createDepthModel(illumina.buildArchitecture(64), synthSeed=0, maxBatch=2)
+    lib = _lib.lib()
+    px = np.zeros((3, 8, 8, 4), np.uint8)
+    h = model._h
+    assert lib.illumina_forward_source(h, px.ctypes.data, 3, 8, 8, None, None, 0, None, None) != 0
+    assert "outside [1, 2]" in lib.illumina_last_error().decode()
+    assert lib.illumina_forward_source(h, px.ctypes.data, 1, 0, 8, None, None, 0, None, None) != 0
+    assert "source size" in lib.illumina_last_error().decode()
+    assert lib.illumina_forward_source(h, px.ctypes.data + 1, 1, 8, 8, None, None, 0, None, None) != 0
+    assert "aligned" in lib.illumina_last_error().decode()
+    assert lib.illumina_forward_source(h, None, 1, 8, 8, None, None, 0, None, None) != 0
+    model.destroy()
