@@ -134,6 +134,12 @@ struct illumina_model {
   float *d_scene = nullptr;
   float *d_tex[2] = {nullptr, nullptr};
   float *d_stage_in = nullptr, *d_stage_out = nullptr, *d_stage_low = nullptr;
+  // illumina_forward_async: two slots of device staging (frames in, disparity
+  // out, allocated on the first asynchronous call) used alternately, so one
+  // call's upload and download overlap its neighbours' graphs
+  float *d_async_in[2] = {nullptr, nullptr}, *d_async_out[2] = {nullptr, nullptr};
+  cudaEvent_t ev_async_in[2] = {}, ev_async_graph[2] = {}, ev_async_out[2] = {};
+  int async_slot = 0;
   // 8-bit source images of a host-buffer illumina_forward_source that do not
   // fit behind the planar frames in d_stage_in (allocated on first need)
   uint8_t *d_src = nullptr;
@@ -187,6 +193,13 @@ illumina_model::~illumina_model() {
   cudaFree(d_stage_out);
   cudaFree(d_stage_low);
   cudaFree(d_src);
+  for (int k = 0; k < 2; k++) {
+    cudaFree(d_async_in[k]);
+    cudaFree(d_async_out[k]);
+    if (ev_async_in[k]) cudaEventDestroy(ev_async_in[k]);
+    if (ev_async_graph[k]) cudaEventDestroy(ev_async_graph[k]);
+    if (ev_async_out[k]) cudaEventDestroy(ev_async_out[k]);
+  }
   cudaFree(d_wimg);
   if (h_err) cudaFreeHost((void *)h_err);
   cudaFree(d_splitk);
@@ -761,6 +774,74 @@ void run_forward_source(illumina_model &m, const uint8_t *rgba8, int n, int w, i
   }
 }
 
+bool is_pinned_host(const void *p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+// An asynchronous forward of pinned host buffers (the reference submits each
+// frame without a fence, src/engine/frame.ts:1-19, and awaits readbacks
+// asynchronously, src/main.ts:572-573):
+// the frames go up on copy_in into one of two device slots, the whole batch
+// runs as one graph on the model stream, the disparity comes down on copy_out;
+// the call returns once that is queued. Consecutive calls alternate slots, so
+// a call's upload and download overlap the neighbouring calls' graphs. The
+// caller's stream is made to wait for the download (the upload does not wait
+// for it); illumina_model_sync waits for everything queued.
+void run_forward_async(illumina_model &m, const float *frames, int n, int layout, float *disp, cudaStream_t caller) {
+  if (n < 1 || n > m.opts.max_batch)
+    throw Error(ILLUMINA_INVALID_ARG, "forwardAsync: batch " + std::to_string(n) + " outside [1, " +
+                                          std::to_string(m.opts.max_batch) + "]");
+  if (layout != ILLUMINA_FRAME_RGB_PLANAR && layout != ILLUMINA_FRAME_RGBA_INTERLEAVED)
+    throw Error(ILLUMINA_INVALID_ARG, "forwardAsync: unknown frame layout " + std::to_string(layout));
+  if (!frames || !disp) throw Error(ILLUMINA_INVALID_ARG, "forwardAsync: frames and disparity are required");
+  cuda_check(cudaSetDevice(m.device), "cudaSetDevice");
+  if (!is_pinned_host(frames) || !is_pinned_host(disp))
+    throw Error(ILLUMINA_INVALID_ARG,
+                "forwardAsync: frames and disparity must be pinned host memory (cudaHostAlloc / cudaHostRegister)");
+  check_timeout(m, "in an earlier call on this model");
+  const int S = m.arch.input_size;
+  const long frame_floats = (layout == ILLUMINA_FRAME_RGB_PLANAR ? 3L : 4L) * S * S;
+  const long disp_floats = (long)S * S;
+  if (!m.d_async_in[0]) {
+    for (int k = 0; k < 2; k++) {
+      cuda_check(cudaMalloc(&m.d_async_in[k], sizeof(float) * 4L * S * S * m.opts.max_batch), "cudaMalloc async");
+      cuda_check(cudaMalloc(&m.d_async_out[k], sizeof(float) * disp_floats * m.opts.max_batch), "cudaMalloc async");
+      cuda_check(cudaEventCreateWithFlags(&m.ev_async_in[k], cudaEventDisableTiming), "event create");
+      cuda_check(cudaEventCreateWithFlags(&m.ev_async_graph[k], cudaEventDisableTiming), "event create");
+      cuda_check(cudaEventCreateWithFlags(&m.ev_async_out[k], cudaEventDisableTiming), "event create");
+    }
+    m.device_bytes += 2 * sizeof(float) * (4L * S * S + disp_floats) * m.opts.max_batch;
+  }
+  const int k = m.async_slot;
+  m.async_slot ^= 1;
+  // upload into slot k once the graph that last read it is done (the frames
+  // are host memory: nothing on the caller's stream precedes them, and
+  // waiting on it would chain each call behind the previous call's download)
+  cuda_check(cudaStreamWaitEvent(m.copy_in, m.ev_async_graph[k], 0), "stream wait");
+  cuda_check(cudaMemcpyAsync(m.d_async_in[k], frames, sizeof(float) * n * frame_floats, cudaMemcpyHostToDevice,
+                             m.copy_in),
+             "frames H2D");
+  cuda_check(cudaEventRecord(m.ev_async_in[k], m.copy_in), "event record");
+  // the graph once the upload is in and the download that last read slot k's output is done
+  cuda_check(cudaStreamWaitEvent(m.stream, m.ev_async_in[k], 0), "stream wait");
+  cuda_check(cudaStreamWaitEvent(m.stream, m.ev_async_out[k], 0), "stream wait");
+  GraphKey key{n, layout, 0, 0, nullptr, nullptr};
+  GraphEntry &g = graph_for(m, key, m.d_async_in[k], m.d_async_out[k], nullptr, nullptr, nullptr);
+  cuda_check(cudaGraphLaunch(g.exec, m.stream), "graph launch");
+  cuda_check(cudaEventRecord(m.ev_async_graph[k], m.stream), "event record");
+  cuda_check(cudaStreamWaitEvent(m.copy_out, m.ev_async_graph[k], 0), "stream wait");
+  cuda_check(cudaMemcpyAsync(disp, m.d_async_out[k], sizeof(float) * n * disp_floats, cudaMemcpyDeviceToHost,
+                             m.copy_out),
+             "disparity D2H");
+  cuda_check(cudaEventRecord(m.ev_async_out[k], m.copy_out), "event record");
+  cuda_check(cudaStreamWaitEvent(caller, m.ev_async_out[k], 0), "caller wait");
+}
+
 void build_model(illumina_model &m, const illumina_model_options &o) {
   m.opts = o;
   if (m.opts.max_batch < 1) throw Error(ILLUMINA_INVALID_ARG, "createDepthModel: max_batch must be >= 1");
@@ -1133,6 +1214,15 @@ illumina_status illumina_forward(illumina_model *m, const float *frames, int n, 
   ILL_CATCH
 }
 
+illumina_status illumina_forward_async(illumina_model *m, const float *frames, int n, int layout, float *disparity,
+                                       void *stream) {
+  ILL_TRY
+  require(m, "forwardAsync: null model");
+  run_forward_async(*m, frames, n, layout, disparity, (cudaStream_t)stream);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
 illumina_status illumina_forward_source(illumina_model *m, const uint8_t *rgba8, int n, int src_w, int src_h,
                                         const float *uv_scale, const float *uv_offset, int mirror, float *disparity,
                                         void *stream) {
@@ -1185,6 +1275,8 @@ illumina_status illumina_model_sync(illumina_model *m) {
   require(m, "sync: null model");
   cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
   cuda_check(cudaStreamSynchronize(m->stream), "synchronize");
+  cuda_check(cudaStreamSynchronize(m->copy_in), "synchronize");
+  cuda_check(cudaStreamSynchronize(m->copy_out), "synchronize");
   check_timeout(*m, "in a forward queued since the last check");
   return ILLUMINA_OK;
   ILL_CATCH

@@ -88,6 +88,18 @@ class DepthModel:
                                      stream_handle(stream)))
         return disparity
 
+    def forwardAsync(self, frames, disparity, stream=None):
+        """forward() without waiting (illumina_forward_async): `frames` and `disparity` are
+        pinned host buffers (numpy views of pinned torch tensors, or pinned CPU tensors) that
+        must stay untouched until sync(); the whole batch runs as one graph while the
+        neighbouring calls' transfers overlap it. Returns `disparity`."""
+        layout, n = self._layout(frames)
+        S = self.arch.inputSize
+        if tuple(disparity.shape) != (n, S, S):
+            raise ValueError(f"disparity must be [{n}, {S}, {S}]")
+        check(lib().illumina_forward_async(self._h, ptr(frames), n, layout, ptr(disparity), stream_handle(stream)))
+        return disparity
+
     def forwardInput(self, inputs, disparity=None, depthLow=None):
         """forwardReference from given network inputs (ref-forward.ts with an "input" bundle):
         [n, S, S, 4] float32 channels-last preprocess outputs. Synchronous; returns the disparity

@@ -648,29 +648,56 @@ def run_ours(args, rank, local_rank, world):
     launches = stats.launches
 
     # ---- end to end through the C ABI with host buffers ----
-    e2e = e2e_rgba8 = None
+    e2e = e2e_sync = e2e_rgba8 = None
     if not args.no_e2e:
         host_in = torch.empty((B, 3, SIZE, SIZE), dtype=torch.float32, pin_memory=True)
         host_in.copy_(frames.cpu())
         host_out = torch.empty((B, SIZE, SIZE), dtype=torch.float32, pin_memory=True)
         hin, hout = host_in.numpy(), host_out.numpy()
+        e_steps = max(3, min(args.steps, 20))
+        # the reference's forward is a queue submission plus an asynchronous
+        # readback: consecutive steps through illumina_forward_async overlap one
+        # step's transfers with the neighbouring steps' graphs; each step still
+        # uploads its frames and downloads its disparity inside the timed region
+        host_out2 = [host_out, torch.empty((B, SIZE, SIZE), dtype=torch.float32, pin_memory=True)]
+        hout2 = [h.numpy() for h in host_out2]
+        for i in range(2):
+            model.forwardAsync(hin, hout2[i], stream=stream)
+        model.sync()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(e_steps):
+            model.forwardAsync(hin, hout2[i % 2], stream=stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        model.sync()
+        barrier()
+        e_ms = max_over_ranks(ev0.elapsed_time(ev1))
+        e2e = {"value": aggregate_frames_per_s(world, B, e_steps, e_ms), "unit": UNIT,
+               "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
+               "steps": e_steps,
+               "path": "illumina_forward_async (C ABI): pinned host buffers, consecutive steps overlapped",
+               "aggregate_pcie_gb_per_s": world * e_steps * (host_in.numel() + host_out.numel()) * 4 / e_ms / 1e6}
+        # the synchronous call, one step at a time (frame chunks overlap within a step)
         for _ in range(2):
             model.forward(hin, disparity=hout, stream=stream)
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
-        e_steps = max(3, min(args.steps, 10))
         ev0.record(stream)
         for _ in range(e_steps):
             model.forward(hin, disparity=hout, stream=stream)
         ev1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        e_ms = max_over_ranks(ev0.elapsed_time(ev1))
-        e2e = {"value": aggregate_frames_per_s(world, B, e_steps, e_ms), "unit": UNIT,
-               "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
-               "steps": e_steps, "path": "illumina_forward (C ABI), pinned host buffers",
-               "aggregate_pcie_gb_per_s": world * e_steps * (host_in.numel() + host_out.numel()) * 4 / e_ms / 1e6}
+        s_ms = max_over_ranks(ev0.elapsed_time(ev1))
+        e2e_sync = {"value": aggregate_frames_per_s(world, B, e_steps, s_ms), "unit": UNIT,
+                    "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
+                    "steps": e_steps, "path": "illumina_forward (C ABI), pinned host buffers, synchronous per step",
+                    "aggregate_pcie_gb_per_s": world * e_steps * (host_in.numel() + host_out.numel()) * 4 / s_ms / 1e6}
+        del host_out2
         # the same frames as 8-bit RGBA source images at the network resolution
         # (the reference's input is an rgba8unorm texture): 4 bytes per pixel
         # cross PCIe instead of 12, sampled on the device by the same call
@@ -784,7 +811,7 @@ def run_ours(args, rank, local_rank, world):
                        "weights": "synthesizeWeights(seed 0)", "parallelism": f"replicas x{world} (frames sharded)",
                        "l2": f"inputs {B * 3 * SIZE * SIZE * 4 / 1e6:.0f} MB per step > 126 MB L2",
                        "precision": args.precision},
-            "e2e": e2e, "e2e_rgba8": e2e_rgba8, "gpu_launches": launches * args.steps, "launches_per_step": launches,
+            "e2e": e2e, "e2e_sync": e2e_sync, "e2e_rgba8": e2e_rgba8, "gpu_launches": launches * args.steps, "launches_per_step": launches,
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), **extras,
             "per_op_ms": {k: round(v, 4) for k, v in per_op.items()} if per_op else None,
         }

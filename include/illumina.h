@@ -180,6 +180,23 @@ illumina_status illumina_forward_source(illumina_model *model, const uint8_t *rg
                                         const float *uv_scale, const float *uv_offset, int mirror, float *disparity,
                                         void *stream);
 
+/* The forward as the reference issues frames (one queue.submit per frame, no
+ * fences, src/engine/frame.ts:1-19; readbacks awaited asynchronously,
+ * src/main.ts:572-573) for pinned host
+ * buffers: queues the upload of `frames` (n frames, `frame_layout`), the
+ * forward of the whole batch as one graph and the download of the disparity
+ * (n x S x S float32) into `disparity`, and returns. Both buffers must be
+ * pinned host memory (cudaHostAlloc / cudaHostRegister) and stay untouched
+ * until the work is done: illumina_model_sync waits for everything queued on
+ * the model; `stream` (nullable) is made to wait for this call's download
+ * (the upload does not wait for `stream`: the frames are host memory).
+ * Consecutive calls alternate two device staging slots (allocated on the first
+ * call, 2 x max_batch x S x S x 5 floats), so one call's transfers overlap the
+ * neighbouring calls' graphs. ILLUMINA_TIMEOUT as for illumina_forward, reported
+ * by the next call or illumina_model_sync. */
+illumina_status illumina_forward_async(illumina_model *model, const float *frames, int n, int frame_layout,
+                                       float *disparity, void *stream);
+
 /* forwardReference from a given network input (scripts/ref-forward.ts:296-300,
  * an "input" bundle; src/model/reference.ts:360-451): `input` holds n x S x S x 4
  * float32 channels-last preprocess outputs (host or device). Runs the stem as
