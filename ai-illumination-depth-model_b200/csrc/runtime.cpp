@@ -139,6 +139,8 @@ struct illumina_model {
   // call's upload and download overlap its neighbours' graphs
   float *d_async_in[2] = {nullptr, nullptr}, *d_async_out[2] = {nullptr, nullptr};
   cudaEvent_t ev_async_in[2] = {}, ev_async_graph[2] = {}, ev_async_out[2] = {};
+  uint8_t *d_async_src[2] = {nullptr, nullptr};  // 8-bit sources too large for a slot's tail
+  size_t d_async_src_bytes = 0;
   int async_slot = 0;
   // 8-bit source images of a host-buffer illumina_forward_source that do not
   // fit behind the planar frames in d_stage_in (allocated on first need)
@@ -196,6 +198,7 @@ illumina_model::~illumina_model() {
   for (int k = 0; k < 2; k++) {
     cudaFree(d_async_in[k]);
     cudaFree(d_async_out[k]);
+    cudaFree(d_async_src[k]);
     if (ev_async_in[k]) cudaEventDestroy(ev_async_in[k]);
     if (ev_async_graph[k]) cudaEventDestroy(ev_async_graph[k]);
     if (ev_async_out[k]) cudaEventDestroy(ev_async_out[k]);
@@ -792,21 +795,40 @@ bool is_pinned_host(const void *p) {
 // a call's upload and download overlap the neighbouring calls' graphs. The
 // caller's stream is made to wait for the download (the upload does not wait
 // for it); illumina_model_sync waits for everything queued.
-void run_forward_async(illumina_model &m, const float *frames, int n, int layout, float *disp, cudaStream_t caller) {
+// The 8-bit source of an asynchronous forward (illumina_forward_source_async).
+struct AsyncSource {
+  const uint8_t *rgba8;
+  int w, h, mirror;
+  const float *uv_scale, *uv_offset;
+};
+
+void run_forward_async(illumina_model &m, const float *frames, int n, int layout, float *disp, cudaStream_t caller,
+                       const AsyncSource *src = nullptr) {
+  const char *who = src ? "forwardSourceAsync" : "forwardAsync";
   if (n < 1 || n > m.opts.max_batch)
-    throw Error(ILLUMINA_INVALID_ARG, "forwardAsync: batch " + std::to_string(n) + " outside [1, " +
+    throw Error(ILLUMINA_INVALID_ARG, std::string(who) + ": batch " + std::to_string(n) + " outside [1, " +
                                           std::to_string(m.opts.max_batch) + "]");
   if (layout != ILLUMINA_FRAME_RGB_PLANAR && layout != ILLUMINA_FRAME_RGBA_INTERLEAVED)
-    throw Error(ILLUMINA_INVALID_ARG, "forwardAsync: unknown frame layout " + std::to_string(layout));
-  if (!frames || !disp) throw Error(ILLUMINA_INVALID_ARG, "forwardAsync: frames and disparity are required");
+    throw Error(ILLUMINA_INVALID_ARG, std::string(who) + ": unknown frame layout " + std::to_string(layout));
+  const void *in = src ? static_cast<const void *>(src->rgba8) : static_cast<const void *>(frames);
+  if (!in || !disp) throw Error(ILLUMINA_INVALID_ARG, std::string(who) + ": input and disparity are required");
+  size_t src_bytes = 0;
+  if (src) {
+    if (src->w < 1 || src->h < 1 || (long)src->w * src->h > (1L << 26))
+      throw Error(ILLUMINA_INVALID_ARG, std::string(who) + ": source size outside [1, 2^26] pixels");
+    if ((reinterpret_cast<uintptr_t>(src->rgba8) & 3) != 0)
+      throw Error(ILLUMINA_INVALID_ARG, std::string(who) + ": rgba8 must be 4-byte aligned");
+    src_bytes = (size_t)src->w * src->h * 4;
+  }
   cuda_check(cudaSetDevice(m.device), "cudaSetDevice");
-  if (!is_pinned_host(frames) || !is_pinned_host(disp))
-    throw Error(ILLUMINA_INVALID_ARG,
-                "forwardAsync: frames and disparity must be pinned host memory (cudaHostAlloc / cudaHostRegister)");
+  if (!is_pinned_host(in) || !is_pinned_host(disp))
+    throw Error(ILLUMINA_INVALID_ARG, std::string(who) +
+                                          ": input and disparity must be pinned host memory (cudaHostAlloc / "
+                                          "cudaHostRegister)");
   check_timeout(m, "in an earlier call on this model");
   const int S = m.arch.input_size;
   const long frame_floats = (layout == ILLUMINA_FRAME_RGB_PLANAR ? 3L : 4L) * S * S;
-  const long disp_floats = (long)S * S;
+  const long planar = 3L * S * S, disp_floats = (long)S * S;
   if (!m.d_async_in[0]) {
     for (int k = 0; k < 2; k++) {
       cuda_check(cudaMalloc(&m.d_async_in[k], sizeof(float) * 4L * S * S * m.opts.max_batch), "cudaMalloc async");
@@ -817,19 +839,48 @@ void run_forward_async(illumina_model &m, const float *frames, int n, int layout
     }
     m.device_bytes += 2 * sizeof(float) * (4L * S * S + disp_floats) * m.opts.max_batch;
   }
+  // a source is staged behind the slot's planar frames when it fits there,
+  // else in per-slot buffers grown on need (after everything queued is done)
+  const size_t tail = sizeof(float) * (size_t)m.opts.max_batch * (4L * S * S - planar);
+  if (src && src_bytes * n > tail && m.d_async_src_bytes < src_bytes * n) {
+    cuda_check(cudaStreamSynchronize(m.stream), "synchronize");
+    cuda_check(cudaStreamSynchronize(m.copy_in), "synchronize");
+    cuda_check(cudaStreamSynchronize(m.copy_out), "synchronize");
+    for (int k = 0; k < 2; k++) {
+      cudaFree(m.d_async_src[k]);
+      m.d_async_src[k] = nullptr;
+    }
+    m.d_async_src_bytes = 0;
+    for (int k = 0; k < 2; k++) cuda_check(cudaMalloc(&m.d_async_src[k], src_bytes * n), "cudaMalloc async source");
+    m.d_async_src_bytes = src_bytes * n;
+  }
   const int k = m.async_slot;
   m.async_slot ^= 1;
-  // upload into slot k once the graph that last read it is done (the frames
-  // are host memory: nothing on the caller's stream precedes them, and
-  // waiting on it would chain each call behind the previous call's download)
+  uint8_t *stage = nullptr;
+  if (src)
+    stage = src_bytes * n <= tail ? reinterpret_cast<uint8_t *>(m.d_async_in[k] + (size_t)m.opts.max_batch * planar)
+                                  : m.d_async_src[k];
+  // upload into slot k once the graph that last read it is done (the input
+  // is host memory: nothing on the caller's stream precedes it, and waiting
+  // on it would chain each call behind the previous call's download)
   cuda_check(cudaStreamWaitEvent(m.copy_in, m.ev_async_graph[k], 0), "stream wait");
-  cuda_check(cudaMemcpyAsync(m.d_async_in[k], frames, sizeof(float) * n * frame_floats, cudaMemcpyHostToDevice,
-                             m.copy_in),
-             "frames H2D");
+  if (src)
+    cuda_check(cudaMemcpyAsync(stage, src->rgba8, src_bytes * n, cudaMemcpyHostToDevice, m.copy_in), "source H2D");
+  else
+    cuda_check(cudaMemcpyAsync(m.d_async_in[k], frames, sizeof(float) * n * frame_floats, cudaMemcpyHostToDevice,
+                               m.copy_in),
+               "frames H2D");
   cuda_check(cudaEventRecord(m.ev_async_in[k], m.copy_in), "event record");
   // the graph once the upload is in and the download that last read slot k's output is done
   cuda_check(cudaStreamWaitEvent(m.stream, m.ev_async_in[k], 0), "stream wait");
   cuda_check(cudaStreamWaitEvent(m.stream, m.ev_async_out[k], 0), "stream wait");
+  if (src) {
+    const float one[2] = {1.0f, 1.0f}, zero[2] = {0.0f, 0.0f};
+    cuda_check(gpu::sample_source(stage, n, src->w, src->h, src->uv_scale ? src->uv_scale : one,
+                                  src->uv_offset ? src->uv_offset : zero, src->mirror ? 1 : 0, S, m.d_async_in[k],
+                                  m.stream),
+               "sample_source");
+  }
   GraphKey key{n, layout, 0, 0, nullptr, nullptr};
   GraphEntry &g = graph_for(m, key, m.d_async_in[k], m.d_async_out[k], nullptr, nullptr, nullptr);
   cuda_check(cudaGraphLaunch(g.exec, m.stream), "graph launch");
@@ -1219,6 +1270,17 @@ illumina_status illumina_forward_async(illumina_model *m, const float *frames, i
   ILL_TRY
   require(m, "forwardAsync: null model");
   run_forward_async(*m, frames, n, layout, disparity, (cudaStream_t)stream);
+  return ILLUMINA_OK;
+  ILL_CATCH
+}
+
+illumina_status illumina_forward_source_async(illumina_model *m, const uint8_t *rgba8, int n, int src_w, int src_h,
+                                              const float *uv_scale, const float *uv_offset, int mirror,
+                                              float *disparity, void *stream) {
+  ILL_TRY
+  require(m, "forwardSourceAsync: null model");
+  const AsyncSource src{rgba8, src_w, src_h, mirror, uv_scale, uv_offset};
+  run_forward_async(*m, nullptr, n, ILLUMINA_FRAME_RGB_PLANAR, disparity, (cudaStream_t)stream, &src);
   return ILLUMINA_OK;
   ILL_CATCH
 }

@@ -102,6 +102,8 @@ SIGNATURES = {
     "illumina_model_record": (_S, [_V, _V, C.c_int, _V]),
     "illumina_forward_input": (_S, [_V, _V, C.c_int, _V, _V]),
     "illumina_forward_async": (_S, [_V, _V, C.c_int, C.c_int, _V, _V]),
+    "illumina_forward_source_async": (_S, [_V, _V, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
+                                          C.POINTER(C.c_float), C.c_int, _V, _V]),
     "illumina_forward_source": (_S, [_V, _V, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_float),
                                     C.c_int, _V, _V]),
     "illumina_model_swap_history": (_S, [_V]),

@@ -100,6 +100,22 @@ class DepthModel:
         check(lib().illumina_forward_async(self._h, ptr(frames), n, layout, ptr(disparity), stream_handle(stream)))
         return disparity
 
+    def forwardSourceAsync(self, rgba8, disparity, uvScale=None, uvOffset=None, mirror: bool = False, stream=None):
+        """forwardSource() without waiting (illumina_forward_source_async): `rgba8` [n, h, w, 4]
+        uint8 and `disparity` [n, S, S] float32 are pinned host buffers that must stay untouched
+        until sync(). Returns `disparity`."""
+        if rgba8.ndim == 3:
+            rgba8 = rgba8[None]
+        n, h, w = int(rgba8.shape[0]), int(rgba8.shape[1]), int(rgba8.shape[2])
+        S = self.arch.inputSize
+        if rgba8.shape[-1] != 4 or tuple(disparity.shape) != (n, S, S):
+            raise ValueError(f"rgba8 must be [n, h, w, 4] and disparity [{n}, {S}, {S}]")
+        sc = (C.c_float * 2)(*(uvScale if uvScale is not None else self.uvScale))
+        of = (C.c_float * 2)(*(uvOffset if uvOffset is not None else self.uvOffset))
+        check(lib().illumina_forward_source_async(self._h, ptr(rgba8), n, w, h, sc, of, int(bool(mirror)),
+                                                  ptr(disparity), stream_handle(stream)))
+        return disparity
+
     def forwardInput(self, inputs, disparity=None, depthLow=None):
         """forwardReference from given network inputs (ref-forward.ts with an "input" bundle):
         [n, S, S, 4] float32 channels-last preprocess outputs. Synchronous; returns the disparity

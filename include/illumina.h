@@ -197,6 +197,16 @@ illumina_status illumina_forward_source(illumina_model *model, const uint8_t *rg
 illumina_status illumina_forward_async(illumina_model *model, const float *frames, int n, int frame_layout,
                                        float *disparity, void *stream);
 
+/* illumina_forward_async for 8-bit RGBA source images: `rgba8` (pinned host,
+ * n images of src_h x src_w x 4 bytes, 4-byte aligned) is uploaded, sampled
+ * as illumina_sample_source does and forwarded; the disparity (pinned host,
+ * n x S x S float32) comes back asynchronously. Sources of up to S x S pixels
+ * are staged in the asynchronous slots; larger ones in two source buffers the
+ * model allocates (or grows, after waiting for its queued work) on need. */
+illumina_status illumina_forward_source_async(illumina_model *model, const uint8_t *rgba8, int n, int src_w,
+                                              int src_h, const float *uv_scale, const float *uv_offset, int mirror,
+                                              float *disparity, void *stream);
+
 /* forwardReference from a given network input (scripts/ref-forward.ts:296-300,
  * an "input" bundle; src/model/reference.ts:360-451): `input` holds n x S x S x 4
  * float32 channels-last preprocess outputs (host or device). Runs the stem as

@@ -66,3 +66,24 @@ def test_async_rejects_pageable_buffers(torch):
     with pytest.raises(illumina.IlluminaError, match="outside"):
         m.forwardAsync(pinned_in.numpy(), pinned_out.numpy())
     m.destroy()
+
+
+@pytest.mark.parametrize("sw,sh", [(S, S), (96, 80)])
+def test_source_async_equals_source_forward(torch, sw, sh):
+    """illumina_forward_source_async over three calls (a 96x80 source does not fit the
+    slots' staging and uses the model's source buffers) equals the synchronous
+    forwardSource of the same images bit for bit (same batch, same graph)."""
+    import illumina
+    n, calls = 4, 3
+    rng = np.random.default_rng(sw)
+    m = illumina.createDepthModel(illumina.buildArchitecture(S), synthSeed=cases.NET64_SEED, maxBatch=n)
+    src = [torch.from_numpy(rng.integers(0, 256, (n, sh, sw, 4), dtype=np.uint8)).pin_memory() for _ in range(calls)]
+    want = [m.forwardSource(s.numpy(), (0.9, 0.8), (0.05, 0.1), True) for s in src]
+    out = [torch.empty((n, S, S), dtype=torch.float32, pin_memory=True) for _ in range(calls)]
+    for i in range(calls):
+        m.forwardSourceAsync(src[i].numpy(), out[i].numpy(), (0.9, 0.8), (0.05, 0.1), True)
+    m.sync()
+    assert m.stats.deviceError == 0
+    for i in range(calls):
+        np.testing.assert_array_equal(out[i].numpy(), want[i])
+    m.destroy()
