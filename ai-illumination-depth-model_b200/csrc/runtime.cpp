@@ -183,6 +183,10 @@ struct illumina_model {
 
 illumina_model::~illumina_model() {
   if (device >= 0) cudaSetDevice(device);
+  // asynchronous forwards may still read or write the staging buffers
+  if (stream) cudaStreamSynchronize(stream);
+  if (copy_in) cudaStreamSynchronize(copy_in);
+  if (copy_out) cudaStreamSynchronize(copy_out);
   clear_graphs();
   cudaFree(d_weights_logical);
   cudaFree(d_weights);
