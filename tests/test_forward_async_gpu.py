@@ -87,3 +87,20 @@ def test_source_async_equals_source_forward(torch, sw, sh):
     for i in range(calls):
         np.testing.assert_array_equal(out[i].numpy(), want[i])
     m.destroy()
+
+
+def test_destroy_waits_for_async_work(torch):
+    """Destroying the model right after an asynchronous call waits for that call:
+    the disparity is complete afterwards."""
+    import illumina
+    n = 2
+    m = illumina.createDepthModel(illumina.buildArchitecture(S), synthSeed=cases.NET64_SEED, maxBatch=n)
+    dev = _frames(torch, n, 7)
+    want = m.forward(dev).cpu().numpy()
+    torch.cuda.synchronize()
+    host_in = torch.empty((n, 3, S, S), dtype=torch.float32, pin_memory=True)
+    host_in.copy_(dev.cpu())
+    host_out = torch.full((n, S, S), -1.0, dtype=torch.float32, pin_memory=True)
+    m.forwardAsync(host_in.numpy(), host_out.numpy())
+    m.destroy()
+    np.testing.assert_array_equal(host_out.numpy(), want)
