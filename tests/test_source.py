@@ -190,17 +190,21 @@ def test_forward_source_rejects_bad_arguments(torch):
 
 @pytest.mark.gpu
 def test_forward_source_fast_upload_schedule(torch):
-    """200 host RGBA8 frames at the network resolution: the chunk schedule for fast
-    uploads (8, 48, 88, 48, 8 frames) against sampling and forwarding the batch on
-    device buffers, within the whole-network tolerance, and bit-identical across calls."""
+    """200 host RGBA8 frames at the network resolution run as the chunks of the
+    fast-upload schedule, 8, 48, 88, 48, 8 frames: bit-identical to sampling and
+    forwarding those chunks one by one on device buffers (a chunk's forward is the
+    forward of its frames alone), and across calls."""
     import illumina
     S, n = 64, 200
     px = np.random.default_rng(200).integers(0, 256, (n, S, S, 4), dtype=np.uint8)
     model = illumina.createDepthModel(illumina.buildArchitecture(S), synthSeed=cases.NET64_SEED, maxBatch=n)
     got = model.forwardSource(px)
     got2 = model.forwardSource(px)
-    want = _device_path(torch, model, px, (1.0, 1.0), (0.0, 0.0), False)
+    want, f0 = [], 0
+    for c in (8, 48, 88, 48, 8):
+        want.append(_device_path(torch, model, px[f0:f0 + c], (1.0, 1.0), (0.0, 0.0), False))
+        f0 += c
     assert model.stats.deviceError == 0
     model.destroy()
     np.testing.assert_array_equal(got2, got)
-    assert float(np.abs(got - want).max()) <= 1e-5
+    np.testing.assert_array_equal(got, np.concatenate(want))
