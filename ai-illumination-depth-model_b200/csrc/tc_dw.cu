@@ -203,6 +203,18 @@ DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const 
   return best;
 }
 
+// Shared memory of tiling `t` for storage type T (the layout plan_tiling costs).
+size_t dw_smem(int T, const DwTiling &t, int KS, const TcWeights &w) {
+  const bool f32 = T == F32;
+  const int terms = f32 ? 2 : 1, slab_c = f32 ? 32 : 64;
+  const size_t dw_bytes = (size_t)(KS * KS + 1) * slab_c * 4;
+  const size_t a_bytes = (size_t)terms * tcx::kAImage, b_bytes = (size_t)terms * w.n_tile * 128;
+  const size_t h_stage = align_to((size_t)t.iw * t.ih * 128 + dw_bytes, 1024);
+  const size_t g_stage = a_bytes + (t.b_res ? 0 : b_bytes);
+  return 1024 + t.sh * h_stage + t.sg * g_stage + (t.b_res ? (size_t)w.n_tiles * w.slabs * b_bytes : 0) +
+         tcd::kEpiBytes + align_to((size_t)w.N * 4, 16) + 8 * (2 * t.sh + 3 * t.sg + 6) + 16;
+}
+
 // plan_tiling is a few-thousand-candidate search; launches of one shape reuse it.
 DwTiling cached_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const TcWeights &w, bool has_res,
                        size_t ws_bytes) {
@@ -246,8 +258,23 @@ cudaError_t tc_dw(int T, const GemmOp &op, const TcWeights &plan, const uint8_t 
   if ((op.ks != 3 && op.ks != 5) || (op.stride != 1 && op.stride != 2)) return cudaErrorInvalidValue;
   auto encode = tensor_map_encoder();
   if (!encode) return cudaErrorNotSupported;
-  const DwTiling tl = cached_tiling(T, op.n, op.OH, op.OW, op.ks, op.stride, plan, op.res != nullptr,
-                                    op.ws ? op.ws_bytes : 0);
+  DwTiling tl = cached_tiling(T, op.n, op.OH, op.OW, op.ks, op.stride, plan, op.res != nullptr,
+                              op.ws ? op.ws_bytes : 0);
+  if (T == BF16 && op.stride == 2) {
+    // stride-2 (expand) ops in bf16 take the patch, groups and rings the fp32
+    // model picks for the same op, which measured 10-35 % faster than the bf16
+    // model's choice (batch 256: e2 0.693 -> 0.482 ms, e4 0.315 -> 0.206,
+    // e6 0.141 -> 0.101, e8 0.102 -> 0.092); the cycle model has no per-item
+    // or shared-memory footprint costs, which decide between these plans
+    const TcWeights w32 = tc_plan_dw(F32, plan.N, plan.K, op.ks);
+    DwTiling t = cached_tiling(F32, op.n, op.OH, op.OW, op.ks, op.stride, w32, op.res != nullptr,
+                               op.ws ? op.ws_bytes : 0);
+    if (t.tw != 0 && t.ksplit == 1) {
+      t.spk = plan.slabs;
+      t.smem = dw_smem(T, t, op.ks, plan);
+      if (t.smem <= kSmemBudget) tl = t;
+    }
+  }
   if (tl.tw == 0) return cudaErrorInvalidValue;
 
   const size_t elt = T == F32 ? 4 : 2;
