@@ -181,10 +181,11 @@ DwTiling plan_tiling(int T, long n_frames, int OH, int OW, int KS, int S, const 
                                                            (std::ceil(ks / 4.0) * 700.0 + 150.0)
                                             : 0.0;
                   // patches of <= 64 pixels (at most half an MMA tile) run slower than the
-                  // model predicts: per-item costs it does not count (measured at batch 256:
-                  // bf16 e5a.dw_project 8x8 patches 0.653 ms, 14x8 0.529 ms; fp32 d2.refine
-                  // 8x8 0.230 ms, the next plan 0.148 ms)
-                  const double small_patch = tw * th <= 64 ? 1.2 : 1.0;
+                  // model predicts when there are waves of items: per-item costs it does not
+                  // count (measured at batch 256: bf16 e5a.dw_project 8x8 patches 0.653 ms,
+                  // 14x8 0.529 ms; fp32 d2.refine 8x8 0.230 ms, the next plan 0.148 ms); with
+                  // fewer items than two waves the small patches' parallelism wins
+                  const double small_patch = tw * th <= 64 && items >= 2 * G ? 1.2 : 1.0;
                   const double cost =
                       (waves * per_unit + red) * (b_res ? 0.99 : 1.0) * (1.0 - 0.001 * (sh + sg)) * small_patch;
                   if (best.tw == 0 || cost < best.cost) {
